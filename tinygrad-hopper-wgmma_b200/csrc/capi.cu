@@ -1,0 +1,546 @@
+// Host side of the sm_100a GEMM behind the C ABI declared in include/sm100_gemm.h.
+//
+// It replaces three host pieces of the reference: the shape/schedule arithmetic of build_gemm_ws and
+// build_gated_gemm (hopper_wgmma/gemm.py:300-319, gated.py:55-63), the tensor-map encoder (tensor_map.py:13-33, here
+// 2-D maps passed as __grid_constant__ kernel parameters instead of 128-byte device tensors), and the
+// process-global tinygrad runtime hooks (runtime.py:20-98), which become explicit launch attributes:
+// cudaFuncSetAttribute for dynamic shared memory and a cluster-dimension attribute on cudaLaunchKernelEx.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <memory>
+#include <mutex>
+#include <vector>
+
+#include "gemm_kernels.cuh"
+#include "sm100_gemm.h"
+
+using sm100::GemmParams;
+
+namespace {
+
+thread_local char g_err[512] = "";
+
+int32_t fail(int32_t code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int32_t cuda_fail(cudaError_t e, const char* what) {
+  return fail(e == cudaSuccess ? 1 : static_cast<int32_t>(e), "%s failed: %s (%s)", what, cudaGetErrorName(e),
+              cudaGetErrorString(e));
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// Driver entry point for cuTensorMapEncodeTiled, fetched through the runtime so that the library does not link
+// libcuda directly (it then loads on machines without a driver, e.g. for the CPU-side tests).
+// ---------------------------------------------------------------------------------------------------------------
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+int32_t encode_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t pitch_elems,
+                  uint32_t box_inner, uint32_t box_outer, const char* what) {
+  auto fn = encode_fn();
+  if (fn == nullptr) return fail(2, "cuTensorMapEncodeTiled is unavailable (no CUDA driver)");
+  const cuuint64_t dims[2] = {inner, outer};
+  const cuuint64_t strides[1] = {pitch_elems * 2};
+  const cuuint32_t box[2] = {box_inner, box_outer};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(3, "cuTensorMapEncodeTiled(%s) failed with CUresult %d", what, static_cast<int>(r));
+  return 0;
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// Tile orders (host). Entries are (row tile << 16) | column tile.
+// ---------------------------------------------------------------------------------------------------------------
+// Hilbert index d -> (x, y) on an n x n grid (n a power of two), the iterative walk used by fast.cu's createHilbert
+// and hilbert_schedule (gemm.py:222-230).
+void hilbert_d2xy(int n, long long d, int& x, int& y) {
+  x = y = 0;
+  long long t = d;
+  for (int s = 1; s < n; s *= 2) {
+    const int rx = static_cast<int>(1 & (t / 2));
+    const int ry = static_cast<int>(1 & (t ^ rx));
+    if (ry == 0) {
+      if (rx == 1) {
+        x = s - 1 - x;
+        y = s - 1 - y;
+      }
+      std::swap(x, y);
+    }
+    x += s * rx;
+    y += s * ry;
+    t /= 4;
+  }
+}
+
+void hilbert_order(int mt, int nt, std::vector<int32_t>& out) {
+  out.clear();
+  int dim = 1;
+  while (dim < std::max(mt, nt)) dim *= 2;
+  for (long long i = 0; i < static_cast<long long>(dim) * dim; ++i) {
+    int x, y;
+    hilbert_d2xy(dim, i, x, y);
+    if (x < mt && y < nt) out.push_back((x << 16) | y);
+  }
+}
+
+// grouped_tile_order (gemm.py:200-215): GM x GN super-tiles in row-major order when they divide the grid, else
+// Triton-style GROUP_M (GM row tiles swept over all columns, column-major inside, ragged last group).
+void grouped_order(int mt, int nt, int gm, int gn, std::vector<int32_t>& out) {
+  out.resize(static_cast<size_t>(mt) * nt);
+  const bool two_d = (mt % gm == 0) && (nt % gn == 0);
+  for (int t = 0; t < mt * nt; ++t) {
+    int r, c;
+    if (two_d) {
+      const int st = t / (gm * gn), pos = t % (gm * gn);
+      r = (st / (nt / gn)) * gm + pos / gn;
+      c = (st % (nt / gn)) * gn + pos % gn;
+    } else {
+      const int first = (t / (gm * nt)) * gm;
+      const int rows = first > mt - gm ? mt - first : gm;
+      const int rr = t % (gm * nt);
+      r = first + rr % rows;
+      c = rr / rows;
+    }
+    out[t] = (r << 16) | c;
+  }
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// Kernel table
+// ---------------------------------------------------------------------------------------------------------------
+using WsKernel = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const GemmParams);
+using RingKernel = void (*)(const CUtensorMap, const CUtensorMap, const GemmParams);
+
+WsKernel pick_ws(int bm, bool paired, bool tma_store) {
+  if (bm == 128) {
+    if (paired) return tma_store ? sm100::sm100_gemm_ws<128, true, true> : sm100::sm100_gemm_ws<128, true, false>;
+    return tma_store ? sm100::sm100_gemm_ws<128, false, true> : sm100::sm100_gemm_ws<128, false, false>;
+  }
+  return tma_store ? sm100::sm100_gemm_ws<64, false, true> : sm100::sm100_gemm_ws<64, false, false>;
+}
+
+RingKernel pick_ring(int bm) { return bm == 128 ? sm100::sm100_gemm_ring<128> : sm100::sm100_gemm_ring<64>; }
+
+uint32_t pow2_cols(int n) {
+  uint32_t c = 32;
+  while (c < static_cast<uint32_t>(n)) c *= 2;
+  return c;
+}
+
+// tcgen05 instruction descriptor, kind::f16: D f32 (bits 4-5 = 1), A bf16 (bits 7-9 = 1), B bf16 (bits 10-12 = 1),
+// both K-major (bits 15, 16 = 0), N >> 3 in bits 17-22, M >> 4 in bits 24-28.
+uint32_t make_idesc(int m, int n) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(n >> 3) << 17) |
+         (static_cast<uint32_t>(m >> 4) << 24);
+}
+
+}  // namespace
+
+struct bg_plan {
+  int device = 0;
+  int kind = BG_KIND_WS;
+  int bm = 128;
+  bool paired = false;
+  bool tma_store = false;
+  int cl = 1;
+  int grid = 0;
+  int threads = 0;
+  size_t smem = 0;
+  int max_active_clusters = 0;
+  CUtensorMap tmA{}, tmB{}, tmC{};
+  GemmParams kp{};
+  int32_t* d_sched = nullptr;
+  unsigned int* d_err = nullptr;
+  WsKernel ws = nullptr;
+  RingKernel ring = nullptr;
+  char name[96] = "";
+};
+
+namespace {
+
+// Save / restore the caller's current device around work on the plan's device.
+struct DeviceGuard {
+  int prev = -1;
+  bool changed = false;
+  cudaError_t status = cudaSuccess;
+  explicit DeviceGuard(int dev) {
+    status = cudaGetDevice(&prev);
+    if (status == cudaSuccess && prev != dev) {
+      status = cudaSetDevice(dev);
+      changed = status == cudaSuccess;
+    }
+  }
+  ~DeviceGuard() {
+    if (changed) cudaSetDevice(prev);
+  }
+};
+
+void free_plan(bg_plan* p) {
+  if (p == nullptr) return;
+  {
+    DeviceGuard g(p->device);
+    if (p->d_sched) cudaFree(p->d_sched);
+    if (p->d_err) cudaFree(p->d_err);
+  }
+  delete p;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* bg_last_error(void) { return g_err; }
+
+int32_t bg_version(void) { return 100; }
+
+int32_t bg_device_info(int32_t device, int32_t* sm_count, int32_t* smem_optin, int32_t* cc_major, int32_t* cc_minor) {
+  int v = 0;
+  cudaError_t e;
+  if ((e = cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, device)) != cudaSuccess)
+    return cuda_fail(e, "cudaDeviceGetAttribute(MultiProcessorCount)");
+  if (sm_count) *sm_count = v;
+  if ((e = cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, device)) != cudaSuccess)
+    return cuda_fail(e, "cudaDeviceGetAttribute(MaxSharedMemoryPerBlockOptin)");
+  if (smem_optin) *smem_optin = v;
+  if ((e = cudaDeviceGetAttribute(&v, cudaDevAttrComputeCapabilityMajor, device)) != cudaSuccess)
+    return cuda_fail(e, "cudaDeviceGetAttribute(ComputeCapabilityMajor)");
+  if (cc_major) *cc_major = v;
+  if ((e = cudaDeviceGetAttribute(&v, cudaDevAttrComputeCapabilityMinor, device)) != cudaSuccess)
+    return cuda_fail(e, "cudaDeviceGetAttribute(ComputeCapabilityMinor)");
+  if (cc_minor) *cc_minor = v;
+  return 0;
+}
+
+int32_t bg_hilbert_order(int32_t m_tiles, int32_t n_tiles, int32_t* out, int32_t capacity) {
+  if (m_tiles <= 0 || n_tiles <= 0 || m_tiles > 0xFFFF || n_tiles > 0xFFFF)
+    return fail(-1, "tile grid %d x %d out of range", m_tiles, n_tiles);
+  std::vector<int32_t> v;
+  hilbert_order(m_tiles, n_tiles, v);
+  if (static_cast<int64_t>(v.size()) > capacity) return fail(-2, "capacity %d < %zu entries", capacity, v.size());
+  std::copy(v.begin(), v.end(), out);
+  return static_cast<int32_t>(v.size());
+}
+
+int32_t bg_grouped_order(int32_t m_tiles, int32_t n_tiles, int32_t group_m, int32_t group_n, int32_t* out,
+                         int32_t capacity) {
+  if (m_tiles <= 0 || n_tiles <= 0 || m_tiles > 0xFFFF || n_tiles > 0xFFFF)
+    return fail(-1, "tile grid %d x %d out of range", m_tiles, n_tiles);
+  if (group_m < 1 || group_n < 1 || group_m > m_tiles || group_n > n_tiles)
+    return fail(-1, "group %d x %d must be within the tile grid %d x %d", group_m, group_n, m_tiles, n_tiles);
+  std::vector<int32_t> v;
+  grouped_order(m_tiles, n_tiles, group_m, group_n, v);
+  if (static_cast<int64_t>(v.size()) > capacity) return fail(-2, "capacity %d < %zu entries", capacity, v.size());
+  std::copy(v.begin(), v.end(), out);
+  return static_cast<int32_t>(v.size());
+}
+
+int32_t bg_encode_tensor_map_3d(void* out128, const void* base, int64_t height, int64_t width, int32_t box_h,
+                                int32_t box_w) {
+  // tensor_map.py:14-17: positive sizes; tile and width multiples of 64 elements.
+  if (box_h <= 0 || box_w <= 0 || height <= 0 || width <= 0) return fail(-1, "tensor-map dimensions must be positive");
+  if (box_w % 64 || width % 64) return fail(-1, "tensor-map tile and width must be multiples of 64 bf16 elements");
+  if (out128 == nullptr || base == nullptr) return fail(-1, "null pointer");
+  auto fn = encode_fn();
+  if (fn == nullptr) return fail(2, "cuTensorMapEncodeTiled is unavailable (no CUDA driver)");
+  const cuuint64_t dims[3] = {64, static_cast<cuuint64_t>(height), static_cast<cuuint64_t>(width / 64)};
+  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(2 * width), 128};
+  const cuuint32_t box[3] = {64, static_cast<cuuint32_t>(box_h), static_cast<cuuint32_t>(box_w / 64)};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(reinterpret_cast<CUtensorMap*>(out128), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base),
+                  dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(3, "cuTensorMapEncodeTiled failed with CUresult %d", static_cast<int>(r));
+  return 0;
+}
+
+int32_t bg_plan_create(bg_plan** out, const bg_cfg* cfg, int64_t M, int64_t N, int64_t K, const void* A, int64_t lda,
+                       const void* BT, int64_t ldb, void* C, int64_t ldc, int32_t device) {
+  if (out == nullptr || cfg == nullptr) return fail(-1, "null plan or cfg pointer");
+  *out = nullptr;
+  const bg_cfg& c = *cfg;
+  // ---- knob validation (gemm.py:260-271, gated.py:27-32)
+  if (c.kind != BG_KIND_WS && c.kind != BG_KIND_GATED && c.kind != BG_KIND_RING)
+    return fail(-1, "unknown kernel kind %d", c.kind);
+  if (c.BK != 64) return fail(-1, "BK must be 64 (one 128-byte swizzle atom)");
+  if (c.BN <= 0 || c.BN % 16 || c.BN > 256) return fail(-1, "BN must be a multiple of 16 in (0, 256]");
+  if (c.tma_store && c.BN % 64) return fail(-1, "tma_store needs BN to be a multiple of 64");
+  if (c.stages != 0 && c.stages < 2) return fail(-1, "stages must be at least 2");
+  if (c.kind == BG_KIND_RING ? c.consumers != 0 : (c.consumers != 1 && c.consumers != 2))
+    return fail(-1, c.kind == BG_KIND_RING ? "the ring kernel has consumers == 0" : "consumers must be 1 or 2");
+  if (c.cluster != 1 && c.cluster != 2) return fail(-1, "cluster must be 1 or 2");
+  if (c.kind != BG_KIND_WS && (c.cluster != 1 || c.hilbert || c.tma_store))
+    return fail(-1, "cluster, hilbert and tma_store need the persistent kernel");
+  if (c.num_sm > 0 && c.num_sm < c.cluster) return fail(-1, "num_sm must be at least the cluster size");
+  if (c.group_m < 1 || c.group_n < 1) return fail(-1, "group_m and group_n must be positive");
+  if (c.acc_bufs < 0 || c.acc_bufs > 2) return fail(-1, "acc_bufs must be 0 (auto), 1 or 2");
+
+  const int bm = 64 * std::max(c.consumers, 1);
+  const int cl = c.cluster;
+  const bool paired = c.kind == BG_KIND_WS && cl == 2 && bm == 128;
+  const int bn = c.BN;
+  const int bn_local = paired ? bn / 2 : bn;
+
+  // ---- shape contract (gemm.py:300-311)
+  if (M <= 0 || N <= 0 || K <= 0) return fail(-1, "M, N and K must be positive");
+  if (M % bm || N % bn || K % 64)
+    return fail(-1, "shape %lldx%lldx%lld not a multiple of tile %dx%dx64", (long long)M, (long long)N, (long long)K, bm,
+                bn);
+  const int64_t mt = M / bm, nt = N / bn, nkb = K / 64;
+  if (mt % cl) return fail(-1, "%lld row tiles not divisible by cluster %d", (long long)mt, cl);
+  const int64_t cmt = mt / cl;
+  if (cmt > 0xFFFF || nt > 0xFFFF || cmt * nt > (1ll << 30) || nkb > (1ll << 30))
+    return fail(-1, "problem too large for the tile table");
+  if (A == nullptr || BT == nullptr || C == nullptr) return fail(-1, "null operand pointer");
+  if ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(BT) | reinterpret_cast<uintptr_t>(C)) & 15)
+    return fail(-1, "operand pointers must be 16-byte aligned");
+  if (lda < K || ldb < K || ldc < N || lda % 8 || ldb % 8 || ldc % 8)
+    return fail(-1, "row pitches must cover the row and be multiples of 8 elements (lda=%lld ldb=%lld ldc=%lld)",
+                (long long)lda, (long long)ldb, (long long)ldc);
+
+  int sm_count = 0, smem_optin = 0, ccmaj = 0, ccmin = 0;
+  int32_t st = bg_device_info(device, &sm_count, &smem_optin, &ccmaj, &ccmin);
+  if (st) return st;
+  if (ccmaj != 10) return fail(4, "device %d is sm_%d%d; this library is built for sm_100a", device, ccmaj, ccmin);
+
+  // ---- shared memory: [A stages][B stages][C staging][barriers], +1024 bytes to align the base
+  const uint32_t a_stage = static_cast<uint32_t>(bm) * 128u;
+  const uint32_t b_stage = static_cast<uint32_t>(bn_local) * 128u;
+  const uint32_t c_bytes = c.tma_store ? static_cast<uint32_t>(bm) * 256u : 0u;
+  const uint32_t fixed = 1024u + c_bytes + (c.kind == BG_KIND_RING ? 16u : 48u);
+  int stages = c.stages;
+  if (stages == 0) {
+    const int64_t fit = (static_cast<int64_t>(smem_optin) - fixed) / (a_stage + b_stage + 16);
+    stages = static_cast<int>(std::min<int64_t>(fit, 8));
+    if (stages < 2) return fail(-1, "not even 2 stages fit in %d bytes of shared memory", smem_optin);
+  }
+  size_t smem = fixed + static_cast<size_t>(stages) * (a_stage + b_stage + 16u);
+  if (smem > static_cast<size_t>(smem_optin))
+    return fail(-1, "needs %zu bytes of shared memory, the limit is %d", smem, smem_optin);
+
+  // ---- accumulators in tensor memory
+  int acc_bufs = c.acc_bufs;
+  if (c.kind != BG_KIND_WS) acc_bufs = 1;
+  if (acc_bufs == 0) acc_bufs = 2 * bn <= 512 ? 2 : 1;
+  if (acc_bufs * bn > 512) return fail(-1, "%d accumulators of %d columns exceed tensor memory", acc_bufs, bn);
+
+  std::unique_ptr<bg_plan, void (*)(bg_plan*)> p(new bg_plan, free_plan);
+  p->device = device;
+  p->kind = c.kind;
+  p->bm = bm;
+  p->paired = paired;
+  p->tma_store = c.tma_store != 0;
+  p->cl = cl;
+  p->smem = smem;
+  p->threads = c.kind == BG_KIND_RING ? sm100::kRingThreads : sm100::kWsThreads;
+
+  DeviceGuard guard(device);
+  if (guard.status != cudaSuccess) return cuda_fail(guard.status, "cudaSetDevice");
+
+  // ---- schedule
+  const int64_t tiles = cmt * nt;
+  int64_t nclusters = tiles;
+  std::vector<int32_t> sched;
+  if (c.kind == BG_KIND_WS) {
+    const int num_sm = c.num_sm > 0 ? c.num_sm : sm_count;
+    nclusters = std::min<int64_t>(num_sm / cl, tiles);
+    if (c.hilbert) {
+      hilbert_order(static_cast<int>(cmt), static_cast<int>(nt), sched);
+    } else {
+      const int gm = std::min<int>(std::max(c.group_m / cl, 1), static_cast<int>(cmt));
+      const int gn = std::min<int>(c.group_n, static_cast<int>(nt));
+      grouped_order(static_cast<int>(cmt), static_cast<int>(nt), gm, gn, sched);
+    }
+  }
+
+  // ---- kernel and launch attributes
+  const void* fn = nullptr;
+  if (c.kind == BG_KIND_RING) {
+    p->ring = pick_ring(bm);
+    fn = reinterpret_cast<const void*>(p->ring);
+  } else {
+    p->ws = pick_ws(bm, paired, p->tma_store);
+    fn = reinterpret_cast<const void*>(p->ws);
+  }
+  cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_optin);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(MaxDynamicSharedMemorySize)");
+  // Tensor memory is 512 columns per SM. CTAs that could share an SM must fit in it together, or a CTA would block
+  // in tcgen05.alloc behind another (and CTA pairs waiting on each other could deadlock). Pad the shared-memory
+  // request until the occupancy limit keeps co-resident CTAs within the SM's tensor memory.
+  {
+    const int tcols = static_cast<int>(pow2_cols(acc_bufs * bn));
+    const int allowed = 512 / tcols;
+    for (;;) {
+      int blocks = 0;
+      e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, fn, p->threads, smem);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
+      if (blocks <= allowed) break;
+      if (smem >= static_cast<size_t>(smem_optin))
+        return fail(5, "cannot limit residency to %d CTAs per SM for %d TMEM columns", allowed, tcols);
+      smem = std::min<size_t>(smem + 8192, static_cast<size_t>(smem_optin));
+    }
+    p->smem = smem;
+  }
+  if (cl > 1) {
+    // Persistent clusters must all be resident at once: cap their number at what the GPU can co-schedule.
+    cudaLaunchConfig_t lc = {};
+    lc.gridDim = dim3(static_cast<unsigned>(cl * nclusters));
+    lc.blockDim = dim3(p->threads);
+    lc.dynamicSmemBytes = smem;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = cl;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    lc.attrs = at;
+    lc.numAttrs = 1;
+    int maxc = 0;
+    e = cudaOccupancyMaxActiveClusters(&maxc, fn, &lc);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveClusters");
+    if (maxc <= 0) return fail(5, "no cluster of %d CTAs with %zu bytes of shared memory fits on the device", cl, smem);
+    p->max_active_clusters = maxc;
+    if (c.kind == BG_KIND_WS) nclusters = std::min<int64_t>(nclusters, maxc);
+  }
+  p->grid = static_cast<int>(nclusters * (c.kind == BG_KIND_RING ? 1 : cl));
+
+  // ---- tensor maps: A[M,K] box (64, BM); BT[N,K] box (64, bn_local); C[M,N] box (64, BM/4) per epilogue warp
+  if ((st = encode_2d(&p->tmA, A, K, M, lda, 64, bm, "A"))) return st;
+  if ((st = encode_2d(&p->tmB, BT, K, N, ldb, 64, bn_local, "BT"))) return st;
+  if (p->tma_store) {
+    if ((st = encode_2d(&p->tmC, C, N, M, ldc, 64, bm / 4, "C"))) return st;
+  } else {
+    p->tmC = p->tmA;   // unused by the register epilogue
+  }
+
+  // ---- device buffers: tile table and error word
+  if (!sched.empty()) {
+    if ((e = cudaMalloc(&p->d_sched, sched.size() * sizeof(int32_t))) != cudaSuccess) return cuda_fail(e, "cudaMalloc");
+    if ((e = cudaMemcpy(p->d_sched, sched.data(), sched.size() * sizeof(int32_t), cudaMemcpyHostToDevice)) != cudaSuccess)
+      return cuda_fail(e, "cudaMemcpy(tile table)");
+  }
+  if ((e = cudaMalloc(&p->d_err, 256)) != cudaSuccess) return cuda_fail(e, "cudaMalloc");
+  if ((e = cudaMemset(p->d_err, 0, 256)) != cudaSuccess) return cuda_fail(e, "cudaMemset");
+
+  GemmParams& kp = p->kp;
+  kp.num_kb = static_cast<int>(nkb);
+  kp.bn = bn;
+  kp.bn_local = bn_local;
+  kp.stages = stages;
+  kp.tiles = static_cast<int>(tiles);
+  kp.nclusters = static_cast<int>(nclusters);
+  kp.cl = c.kind == BG_KIND_RING ? 1 : cl;
+  kp.nt = static_cast<int>(nt);
+  kp.acc_bufs = acc_bufs;
+  kp.acc_stride = bn;
+  kp.tmem_cols = pow2_cols(acc_bufs * bn);
+  kp.idesc = make_idesc(paired ? 2 * bm : bm, bn);
+  kp.tx_bytes = (a_stage + b_stage) * (paired ? 2u : 1u);
+  kp.a_stage_bytes = a_stage;
+  kp.b_stage_bytes = b_stage;
+  kp.sched = p->d_sched;
+  kp.C = static_cast<__nv_bfloat16*>(C);
+  kp.ldc = ldc;
+  kp.err = p->d_err;
+  kp.budget_ns = c.wait_budget_ns > 0 ? static_cast<unsigned long long>(c.wait_budget_ns) : 4000000000ull;
+  kp.skip_job = c.debug_skip_job;
+
+  snprintf(p->name, sizeof(p->name), "%s<BM=%d,%s,%s> BN=%d stages=%d acc=%d", c.kind == BG_KIND_RING ? "sm100_gemm_ring" : "sm100_gemm_ws",
+           bm, paired ? "pair" : (cl == 2 ? "cluster2" : "cta"), p->tma_store ? "tma_store" : "reg_store", bn, stages,
+           acc_bufs);
+  *out = p.release();
+  return 0;
+}
+
+int32_t bg_plan_launch(bg_plan* p, void* stream) {
+  if (p == nullptr) return fail(-1, "null plan");
+  DeviceGuard guard(p->device);
+  if (guard.status != cudaSuccess) return cuda_fail(guard.status, "cudaSetDevice");
+  cudaLaunchConfig_t lc = {};
+  lc.gridDim = dim3(static_cast<unsigned>(p->grid));
+  lc.blockDim = dim3(static_cast<unsigned>(p->threads));
+  lc.dynamicSmemBytes = p->smem;
+  lc.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute at[1];
+  lc.attrs = at;
+  lc.numAttrs = 0;
+  if (p->cl > 1 && p->kind == BG_KIND_WS) {
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = p->cl;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    lc.numAttrs = 1;
+  }
+  cudaError_t e;
+  if (p->kind == BG_KIND_RING)
+    e = cudaLaunchKernelEx(&lc, p->ring, p->tmA, p->tmB, p->kp);
+  else
+    e = cudaLaunchKernelEx(&lc, p->ws, p->tmA, p->tmB, p->tmC, p->kp);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaLaunchKernelEx");
+  return 0;
+}
+
+int32_t bg_plan_check_error(bg_plan* p, void* stream, uint32_t* err_word) {
+  if (p == nullptr) return fail(-1, "null plan");
+  DeviceGuard guard(p->device);
+  if (guard.status != cudaSuccess) return cuda_fail(guard.status, "cudaSetDevice");
+  cudaError_t e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaStreamSynchronize");
+  uint32_t w = 0;
+  if ((e = cudaMemcpy(&w, p->d_err, sizeof(w), cudaMemcpyDeviceToHost)) != cudaSuccess)
+    return cuda_fail(e, "cudaMemcpy(error word)");
+  if (err_word) *err_word = w;
+  if (w != 0) {
+    cudaMemset(p->d_err, 0, sizeof(uint32_t));
+    static const char* roles[] = {"?", "producer (free stage)", "MMA (loaded stage)", "MMA (free accumulator)",
+                                  "epilogue (finished accumulator)", "MMA drain", "load drain"};
+    const uint32_t role = w >> 24;
+    return fail(6, "device wait timed out: %s, counter %u (error word 0x%08x)", role < 7 ? roles[role] : "?",
+                w & 0xFFFFFFu, w);
+  }
+  return 0;
+}
+
+int32_t bg_plan_get_info(const bg_plan* p, bg_plan_info* info) {
+  if (p == nullptr || info == nullptr) return fail(-1, "null pointer");
+  info->grid = p->grid;
+  info->threads = p->threads;
+  info->smem_bytes = static_cast<int32_t>(p->smem);
+  info->stages = p->kp.stages;
+  info->tiles = p->kp.tiles;
+  info->clusters = p->kp.nclusters;
+  info->cluster = p->cl;
+  info->paired = p->paired ? 1 : 0;
+  info->bm = p->bm;
+  info->bn = p->kp.bn;
+  info->acc_bufs = p->kp.acc_bufs;
+  info->tmem_cols = static_cast<int32_t>(p->kp.tmem_cols);
+  info->max_active_clusters = p->max_active_clusters;
+  snprintf(info->kernel, sizeof(info->kernel), "%s", p->name);
+  return 0;
+}
+
+void bg_plan_destroy(bg_plan* p) { free_plan(p); }
+
+}  // extern "C"

@@ -1,0 +1,473 @@
+// bf16 GEMM kernels for sm_100a: C[M,N] = A[M,K] * B[K,N], operands K-major (A row-major, B given as BT[N,K]),
+// fp32 accumulation in tensor memory, bf16 output, every dimension a multiple of the tile.
+//
+//   sm100_gemm_ws    warp-specialized tcgen05 GEMM. Used for the reference's persistent ladder rungs
+//                    (hopper_wgmma/gemm.py:293-398: role_split, tma_store, hilbert, cluster, cluster_hilbert) with
+//                    one cluster per SM and a host-built tile table, and for the non-persistent warp-specialized
+//                    rung (hopper_wgmma/gated.py:50-123 with consumers >= 1) with one tile per cluster.
+//   sm100_gemm_ring  one thread issues both the TMA ring and the MMAs, one tile per CTA: the reference's "ring only"
+//                    rung (gated.py with consumers = 0, ladder.py:8).
+//
+// Warp roles of sm100_gemm_ws (256 threads):
+//   warp 0, lane 0   TMA producer: for every (tile, k-block) it waits for a free shared-memory stage, then loads the
+//                    A tile (BM x 64) and its B tile (bn_local x 64) with 128-byte swizzle.
+//   warp 1           allocates tensor memory; lane 0 issues tcgen05.mma (4 x K16 per stage) into one of two
+//                    accumulator buffers and commits stage releases and "accumulator full" events to mbarriers.
+//   warps 4-7        epilogue: warp w owns TMEM lane quadrant w % 4 (32 accumulator rows, or 16 for BM = 64),
+//                    reads fp32 columns with tcgen05.ld, rounds to bf16 and writes C either directly
+//                    (register epilogue) or through a 128B-swizzled staging buffer and a TMA store (per warp,
+//                    double-buffered), then frees the accumulator buffer for the next tile.
+// In a CTA pair (PAIRED, cta_group::2) both CTAs load their own A rows and their own half of the B tile; only the
+// even CTA issues MMAs (M = 256 across the pair); the odd CTA's loads complete on the even CTA's barriers and the
+// MMA commits arrive on both CTAs' barriers. No load is multicast.
+//
+// Every mbarrier wait is bounded (GemmParams::budget_ns). On expiry a thread writes a code into GemmParams::err and
+// leaves its loop; all other roles then run out of work or time out too, the kernel drains what it issued, frees
+// its tensor memory and returns, and the host turns the code into an error.
+#pragma once
+#include "ptx.cuh"
+
+namespace sm100 {
+
+constexpr int kBK = 64;           // K per pipeline stage: one 128-byte swizzle row of bf16
+constexpr int kWsThreads = 256;   // warps 0-3 producer / MMA / idle, warps 4-7 epilogue
+constexpr int kRingThreads = 128;
+
+// Error word layout: role in bits 24-31, the role's job or tile counter (saturated) in bits 0-23.
+enum : uint32_t {
+  kErrProducer = 1u << 24,    // producer timed out waiting for a free stage
+  kErrMmaFull = 2u << 24,     // MMA issuer timed out waiting for a loaded stage
+  kErrMmaAcc = 3u << 24,      // MMA issuer timed out waiting for a free accumulator buffer
+  kErrEpilogue = 4u << 24,    // epilogue timed out waiting for a finished accumulator
+  kErrDrain = 5u << 24,       // final wait for outstanding MMAs timed out
+  kErrLoadDrain = 6u << 24,   // producer's final wait for its in-flight loads timed out (after another error)
+};
+
+struct GemmParams {
+  int num_kb;              // K / 64
+  int bn;                  // MMA N: output columns per tile (the whole pair's tile when PAIRED)
+  int bn_local;            // rows of BT this CTA loads per stage (bn / 2 when PAIRED)
+  int stages;              // shared-memory ring depth
+  int tiles;               // schedule entries (cluster tiles)
+  int nclusters;           // clusters (persistent workers) in the grid
+  int cl;                  // CTAs per cluster (1 or 2)
+  int nt;                  // column tiles; used when sched == nullptr (row-major tile order)
+  int acc_bufs;            // accumulator buffers in tensor memory (1 or 2)
+  int acc_stride;          // TMEM columns between accumulator buffers
+  uint32_t tmem_cols;      // TMEM columns allocated (power of two >= 32)
+  uint32_t idesc;          // tcgen05 instruction descriptor (bf16 x bf16 -> f32, K-major, M, N)
+  uint32_t tx_bytes;       // bytes that complete one stage's FULL barrier (both CTAs' loads when PAIRED)
+  uint32_t a_stage_bytes;  // BM * 128
+  uint32_t b_stage_bytes;  // bn_local * 128
+  const int32_t* sched;    // [tiles] entries (cluster row tile << 16) | column tile; entry i runs on cluster
+                           // i % nclusters as that cluster's (i / nclusters)-th tile
+  __nv_bfloat16* C;        // output base (register epilogue)
+  long long ldc;           // C row pitch in elements
+  unsigned int* err;       // error word (0 = ok)
+  unsigned long long budget_ns;  // per-wait time limit
+  int skip_job;            // test hook: the producer never loads this job index (-1 = off); makes waits run out
+};
+
+__device__ __forceinline__ void record_error(unsigned int* err, uint32_t role, uint32_t counter) {
+  atomicCAS(err, 0u, role | (counter > 0xFFFFFFu ? 0xFFFFFFu : counter));
+}
+
+__device__ __forceinline__ void tile_coords(const GemmParams& p, int idx, int& cm, int& tn) {
+  if (p.sched != nullptr) {
+    const int e = __ldg(p.sched + idx);
+    cm = e >> 16;
+    tn = e & 0xFFFF;
+  } else {
+    cm = idx / p.nt;
+    tn = idx - cm * p.nt;
+  }
+}
+
+// Round 2N fp32 accumulator words to bf16 and store N/2 packed words per 16-byte chunk.
+template <int N>
+__device__ __forceinline__ void store_row_global(__nv_bfloat16* dst, const uint32_t (&v)[N]) {
+#pragma unroll
+  for (int j = 0; j < N / 8; ++j)
+    st_global_v4(dst + 8 * j, pack_bf16x2(v[8 * j + 0], v[8 * j + 1]), pack_bf16x2(v[8 * j + 2], v[8 * j + 3]),
+                 pack_bf16x2(v[8 * j + 4], v[8 * j + 5]), pack_bf16x2(v[8 * j + 6], v[8 * j + 7]));
+}
+
+// Register epilogue for one accumulator: this thread's row, columns [0, bn), 32 at a time plus a 16-column tail.
+__device__ __forceinline__ void epilogue_registers(uint32_t tacc, __nv_bfloat16* crow, int bn, bool active) {
+  const int n32 = bn >> 5;
+#pragma unroll 1
+  for (int c = 0; c < n32; ++c) {
+    uint32_t v[32];
+    tmem_ld_32x32b_x32(tacc + 32 * c, v);
+    tmem_ld_wait();
+    if (active) store_row_global<32>(crow + 32 * c, v);
+  }
+  if (bn & 16) {
+    uint32_t v[16];
+    tmem_ld_32x32b_x16(tacc + 32 * n32, v);
+    tmem_ld_wait();
+    if (active) store_row_global<16>(crow + 32 * n32, v);
+  }
+}
+
+template <int BM, bool PAIRED, bool TMA_STORE>
+__global__ void __launch_bounds__(kWsThreads, 1)
+    sm100_gemm_ws(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                  const __grid_constant__ CUtensorMap tmC, const GemmParams p) {
+  static_assert(BM == 64 || BM == 128, "BM is 64 or 128 rows per CTA");
+  static_assert(!PAIRED || BM == 128, "CTA pairs use M = 256 (128 rows per CTA)");
+  constexpr int CG = PAIRED ? 2 : 1;
+  constexpr int ROWS_W = BM / 4;                  // accumulator rows per epilogue warp
+  constexpr uint32_t STAGE_C = ROWS_W * 128;      // one 64-column bf16 staging buffer of one warp
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;   // 128B-swizzled tiles need 1024-byte alignment
+  const uint32_t sA = base;
+  const uint32_t sB = sA + p.stages * p.a_stage_bytes;
+  const uint32_t sC = sB + p.stages * p.b_stage_bytes;
+  const uint32_t bars = sC + (TMA_STORE ? 4u * 2u * STAGE_C : 0u);
+  const uint32_t full0 = bars;
+  const uint32_t empty0 = bars + 8u * p.stages;
+  const uint32_t tfull0 = bars + 16u * p.stages;
+  const uint32_t tempty0 = tfull0 + 16u;
+  const uint32_t drain = tempty0 + 16u;
+  const uint32_t tslot = drain + 8u;
+  volatile uint32_t* tslot_ptr = reinterpret_cast<volatile uint32_t*>(smem_raw + (tslot - raw));
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = p.cl > 1 ? cluster_ctarank() : 0u;
+  const int cid = static_cast<int>(blockIdx.x) / p.cl;
+  const bool leader = !PAIRED || rank == 0;
+  const uint64_t budget = p.budget_ns;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < p.stages; ++s) {
+      mbar_init(full0 + 8u * s, 1);
+      mbar_init(empty0 + 8u * s, 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(tfull0 + 8u * b, 1);
+      mbar_init(tempty0 + 8u * b, 4 * CG);   // one arrival per epilogue warp of each CTA of the pair
+    }
+    mbar_init(drain, 1);
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_map(&tmA);
+    tma_prefetch_map(&tmB);
+    if (TMA_STORE) tma_prefetch_map(&tmC);
+  }
+  if (warp == 1) {
+    tmem_alloc<CG>(tslot, p.tmem_cols);
+    tmem_relinquish<CG>();
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (PAIRED) cluster_sync_all();   // the peer's barriers and TMEM exist before anyone signals them
+  tc_fence_after();
+  const uint32_t tmem_base = *tslot_ptr;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      uint32_t stage = 0, phase = 0;
+      int job = 0;
+      bool failed = false;
+      for (int i = 0; !failed; ++i) {
+        const int idx = cid + i * p.nclusters;
+        if (idx >= p.tiles) break;
+        int cm, tn;
+        tile_coords(p, idx, cm, tn);
+        const int row_a = (cm * p.cl + static_cast<int>(rank)) * BM;
+        const int row_b = tn * p.bn + (PAIRED ? static_cast<int>(rank) * p.bn_local : 0);
+        for (int kb = 0; kb < p.num_kb; ++kb, ++job) {
+          if (!mbar_wait_bounded(empty0 + 8u * stage, phase ^ 1u, budget)) {
+            record_error(p.err, kErrProducer, job);
+            failed = true;
+            break;
+          }
+          if (job != p.skip_job) {
+            const uint32_t fb = full0 + 8u * stage;
+            if (PAIRED) {
+              const uint32_t fb_leader = mapa_shared(fb, 0);
+              if (leader) mbar_arrive_expect_tx(fb, p.tx_bytes);
+              tma_load_2d_pair(sA + stage * p.a_stage_bytes, &tmA, fb_leader, kb * kBK, row_a);
+              tma_load_2d_pair(sB + stage * p.b_stage_bytes, &tmB, fb_leader, kb * kBK, row_b);
+            } else {
+              mbar_arrive_expect_tx(fb, p.tx_bytes);
+              tma_load_2d(sA + stage * p.a_stage_bytes, &tmA, fb, kb * kBK, row_a);
+              tma_load_2d(sB + stage * p.b_stage_bytes, &tmB, fb, kb * kBK, row_b);
+            }
+          }
+          if (++stage == static_cast<uint32_t>(p.stages)) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (leader) {
+        // Let the loads already issued land before shared memory goes away: the newest job of every stage. On the
+        // normal path the MMA has consumed them all and these waits return at once; after an error elsewhere they
+        // keep the CTA alive until its own copies have arrived. (A pair's FULL barriers live in the even CTA and
+        // count both CTAs' bytes; the odd CTA leaves only after the cluster barrier below.)
+        const int first = job - p.stages < 0 ? 0 : job - p.stages;
+        for (int j = first; j < job; ++j) {
+          if (j == p.skip_job) continue;
+          const uint32_t s = static_cast<uint32_t>(j % p.stages), ph = static_cast<uint32_t>((j / p.stages) & 1);
+          if (!mbar_wait_bounded(full0 + 8u * s, ph, budget)) record_error(p.err, kErrLoadDrain, j);
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0 && leader) {
+      uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
+      int job = 0;
+      bool failed = false;
+      for (int i = 0; !failed; ++i) {
+        const int idx = cid + i * p.nclusters;
+        if (idx >= p.tiles) break;
+        if (!mbar_wait_bounded(tempty0 + 8u * acc, acc_phase ^ 1u, budget)) {
+          record_error(p.err, kErrMmaAcc, i);
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem_base + acc * static_cast<uint32_t>(p.acc_stride);
+        for (int kb = 0; kb < p.num_kb; ++kb, ++job) {
+          if (!mbar_wait_bounded(full0 + 8u * stage, phase, budget)) {
+            record_error(p.err, kErrMmaFull, job);
+            failed = true;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t ad = smem_desc_sw128(sA + stage * p.a_stage_bytes);
+          const uint64_t bd = smem_desc_sw128(sB + stage * p.b_stage_bytes);
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k)   // +32 bytes along K inside the swizzle row = +2 in the address field
+            mma_bf16<CG>(d, ad + 2u * k, bd + 2u * k, p.idesc, (kb | k) != 0 ? 1u : 0u);
+          mma_commit<CG>(empty0 + 8u * stage);
+          if (PAIRED) mma_commit<CG>(mapa_shared(empty0 + 8u * stage, 1));
+          if (++stage == static_cast<uint32_t>(p.stages)) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (failed) break;
+        mma_commit<CG>(tfull0 + 8u * acc);
+        if (PAIRED) mma_commit<CG>(mapa_shared(tfull0 + 8u * acc, 1));
+        if (++acc == static_cast<uint32_t>(p.acc_bufs)) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
+      }
+      mma_commit<CG>(drain);   // every MMA issued above has finished once this arrives
+      if (!mbar_wait_bounded(drain, 0, budget)) record_error(p.err, kErrDrain, 0);
+    }
+    __syncwarp();
+  } else if (warp >= 4) {
+    // ------------------------------------------------------------------ epilogue
+    const int q = warp & 3;   // TMEM lane quadrant this warp may access
+    const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
+    const uint32_t my_stage = sC + static_cast<uint32_t>(q) * 2u * STAGE_C;
+    uint32_t acc = 0, acc_phase = 0, chunk = 0;
+    for (int i = 0;; ++i) {
+      const int idx = cid + i * p.nclusters;
+      if (idx >= p.tiles) break;
+      int cm, tn;
+      tile_coords(p, idx, cm, tn);
+      const int row0 = (cm * p.cl + static_cast<int>(rank)) * BM + q * ROWS_W;   // first row of this warp
+      const int col0 = tn * p.bn;
+      if (!mbar_wait_bounded(tfull0 + 8u * acc, acc_phase, budget)) {
+        record_error(p.err, kErrEpilogue, i);
+        break;
+      }
+      tc_fence_after();
+      const uint32_t tacc = tmem_base + lane_base + acc * static_cast<uint32_t>(p.acc_stride);
+      if constexpr (TMA_STORE) {
+        const int nchunks = p.bn >> 6;
+#pragma unroll 1
+        for (int c = 0; c < nchunks; ++c, ++chunk) {
+          uint32_t v0[32], v1[32];
+          tmem_ld_32x32b_x32(tacc + 64u * c, v0);
+          tmem_ld_32x32b_x32(tacc + 64u * c + 32u, v1);
+          tmem_ld_wait();
+          const uint32_t buf = my_stage + (chunk & 1u) * STAGE_C;
+          if (lane == 0) bulk_wait_group_read<1>();   // the store issued from this buffer two chunks ago has read it
+          __syncwarp();
+          if (lane < ROWS_W) {
+            // row `lane` of the staging tile: 16-byte chunk j holds columns 8j..8j+7, stored at chunk j ^ (row % 8)
+            const uint32_t rowaddr = buf + static_cast<uint32_t>(lane) * 128u;
+            const uint32_t sw = static_cast<uint32_t>(lane) & 7u;
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              st_shared_v4(rowaddr + ((static_cast<uint32_t>(j) ^ sw) << 4), pack_bf16x2(v0[8 * j], v0[8 * j + 1]),
+                           pack_bf16x2(v0[8 * j + 2], v0[8 * j + 3]), pack_bf16x2(v0[8 * j + 4], v0[8 * j + 5]),
+                           pack_bf16x2(v0[8 * j + 6], v0[8 * j + 7]));
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              st_shared_v4(rowaddr + ((static_cast<uint32_t>(j + 4) ^ sw) << 4), pack_bf16x2(v1[8 * j], v1[8 * j + 1]),
+                           pack_bf16x2(v1[8 * j + 2], v1[8 * j + 3]), pack_bf16x2(v1[8 * j + 4], v1[8 * j + 5]),
+                           pack_bf16x2(v1[8 * j + 6], v1[8 * j + 7]));
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&tmC, buf, col0 + 64 * c, row0);
+            bulk_commit_group();
+          }
+        }
+      } else {
+        __nv_bfloat16* crow = p.C + static_cast<long long>(row0 + lane) * p.ldc + col0;
+        epilogue_registers(tacc, crow, p.bn, lane < ROWS_W);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        if (PAIRED)
+          mbar_arrive_cluster(mapa_shared(tempty0 + 8u * acc, 0));
+        else
+          mbar_arrive_local(tempty0 + 8u * acc);
+      }
+      if (++acc == static_cast<uint32_t>(p.acc_bufs)) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+    }
+    if (TMA_STORE && lane == 0) bulk_wait_group<0>();
+    __syncwarp();
+  }
+
+  // ------------------------------------------------------------------ teardown
+  tc_fence_before();
+  __syncthreads();
+  if (PAIRED) cluster_sync_all();   // the pair is done with each other's barriers and tensor memory
+  tc_fence_after();
+  if (warp == 1) {
+    __syncwarp();
+    tmem_dealloc<CG>(tmem_base, p.tmem_cols);
+  }
+}
+
+// One thread runs the whole mainloop: a prologue fills the ring, then each k-block waits for its stage, issues the
+// MMAs, commits the stage's release and, once the MMA has read it, refills the stage with the k-block `stages`
+// ahead. All four warps then drain the accumulator with the register epilogue. One tile per CTA, row-major order.
+template <int BM>
+__global__ void __launch_bounds__(kRingThreads, 1)
+    sm100_gemm_ring(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                    const GemmParams p) {
+  constexpr int ROWS_W = BM / 4;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  const uint32_t sA = base;
+  const uint32_t sB = sA + p.stages * p.a_stage_bytes;
+  const uint32_t bars = sB + p.stages * p.b_stage_bytes;
+  const uint32_t full0 = bars;
+  const uint32_t empty0 = bars + 8u * p.stages;
+  const uint32_t tfull = bars + 16u * p.stages;
+  const uint32_t tslot = tfull + 8u;
+  volatile uint32_t* tslot_ptr = reinterpret_cast<volatile uint32_t*>(smem_raw + (tslot - raw));
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint64_t budget = p.budget_ns;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < p.stages; ++s) {
+      mbar_init(full0 + 8u * s, 1);
+      mbar_init(empty0 + 8u * s, 1);
+    }
+    mbar_init(tfull, 1);
+    fence_mbar_init();
+    tma_prefetch_map(&tmA);
+    tma_prefetch_map(&tmB);
+  }
+  if (warp == 0) {
+    tmem_alloc<1>(tslot, p.tmem_cols);
+    tmem_relinquish<1>();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tslot_ptr;
+
+  int cm, tn;
+  tile_coords(p, static_cast<int>(blockIdx.x), cm, tn);
+  const int row_a = cm * BM;
+  const int row_b = tn * p.bn;
+
+  if (threadIdx.x == 0) {
+    const int pro = p.num_kb < p.stages ? p.num_kb : p.stages;
+    for (int j = 0; j < pro; ++j) {
+      if (j == p.skip_job) continue;
+      mbar_arrive_expect_tx(full0 + 8u * j, p.tx_bytes);
+      tma_load_2d(sA + j * p.a_stage_bytes, &tmA, full0 + 8u * j, j * kBK, row_a);
+      tma_load_2d(sB + j * p.b_stage_bytes, &tmB, full0 + 8u * j, j * kBK, row_b);
+    }
+    bool failed = false;
+    int issued = pro;   // loads issued so far (jobs 0 .. issued-1)
+    for (int kb = 0; kb < p.num_kb; ++kb) {
+      const uint32_t s = static_cast<uint32_t>(kb % p.stages), ph = static_cast<uint32_t>((kb / p.stages) & 1);
+      if (!mbar_wait_bounded(full0 + 8u * s, ph, budget)) {
+        record_error(p.err, kErrMmaFull, kb);
+        failed = true;
+        break;
+      }
+      tc_fence_after();
+      const uint64_t ad = smem_desc_sw128(sA + s * p.a_stage_bytes);
+      const uint64_t bd = smem_desc_sw128(sB + s * p.b_stage_bytes);
+#pragma unroll
+      for (int k = 0; k < kBK / 16; ++k) mma_bf16<1>(tmem_base, ad + 2u * k, bd + 2u * k, p.idesc, (kb | k) != 0);
+      mma_commit<1>(empty0 + 8u * s);
+      const int nxt = kb + p.stages;
+      if (nxt < p.num_kb) {
+        if (!mbar_wait_bounded(empty0 + 8u * s, ph, budget)) {   // the MMAs above have read stage s
+          record_error(p.err, kErrProducer, nxt);
+          failed = true;
+          break;
+        }
+        if (nxt != p.skip_job) {
+          mbar_arrive_expect_tx(full0 + 8u * s, p.tx_bytes);
+          tma_load_2d(sA + s * p.a_stage_bytes, &tmA, full0 + 8u * s, nxt * kBK, row_a);
+          tma_load_2d(sB + s * p.b_stage_bytes, &tmB, full0 + 8u * s, nxt * kBK, row_b);
+        }
+        issued = nxt + 1;
+      }
+    }
+    mma_commit<1>(tfull);   // also the drain point for every MMA issued above
+    if (failed) {
+      const int first = issued - p.stages < 0 ? 0 : issued - p.stages;
+      for (int j = first; j < issued; ++j) {
+        if (j == p.skip_job) continue;
+        const uint32_t s = static_cast<uint32_t>(j % p.stages), ph = static_cast<uint32_t>((j / p.stages) & 1);
+        if (!mbar_wait_bounded(full0 + 8u * s, ph, budget)) record_error(p.err, kErrLoadDrain, j);
+      }
+    }
+  }
+  __syncwarp();
+
+  const bool ready = mbar_wait_bounded(tfull, 0, budget);
+  if (!ready) record_error(p.err, kErrEpilogue, 0);
+  tc_fence_after();
+  __syncwarp();
+  {
+    const int q = warp & 3;
+    const uint32_t tacc = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
+    __nv_bfloat16* crow = p.C + static_cast<long long>(row_a + q * ROWS_W + lane) * p.ldc + row_b;
+    // A failed tile leaves C unwritten (the host reports the error), but the TMEM reads stay warp-uniform.
+    epilogue_registers(tacc, crow, p.bn, ready && lane < ROWS_W);
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 0) {
+    __syncwarp();
+    tmem_dealloc<1>(tmem_base, p.tmem_cols);
+  }
+}
+
+}  // namespace sm100

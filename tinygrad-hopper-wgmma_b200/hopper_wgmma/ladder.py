@@ -1,0 +1,42 @@
+"""The optimization ladder as named configs (the reference's hopper_wgmma/ladder.py:7-37), on B200.
+
+Names and knob combinations are the reference's. Knobs the reference hard-coded for an H200 are left at their
+B200 defaults: ``num_sm`` is the device's SM count and ``stages`` fills shared memory."""
+from __future__ import annotations
+
+from .gated import GatedCfg, build_gated_gemm
+from .gemm import WSCfg, build_gemm_ws
+
+LADDER = {
+  "tma_ring": GatedCfg(BN=128, stages=4, consumers=0),            # one thread drives the TMA ring and the MMAs
+  "gated_ws": GatedCfg(consumers=2),                              # warp specialization, one tile per CTA
+  "role_split": WSCfg(),                                          # persistent, role-split, 16x8 tile order
+  "role_split_regs": WSCfg(regs=(24, 240)),                       # role_split + register split knob
+  "tma_store": WSCfg(tma_store=True),                             # + swizzled staging / TMA-store epilogue
+  "hilbert": WSCfg(tma_store=True, hilbert=True),                 # + Hilbert tile order
+  "cluster": WSCfg(tma_store=True, cluster=2),                    # CTA pairs on cta_group::2 (instead of Hilbert)
+  "cluster_hilbert": WSCfg(tma_store=True, hilbert=True, cluster=2),
+}
+
+
+def build(N: int, cfg, M: int | None = None, K: int | None = None, **hooks):
+  """Build the right GEMM for ``cfg``. Gated configs are square only."""
+  if isinstance(cfg, GatedCfg):
+    if (M, K) not in ((None, None), (N, N)): raise ValueError("the gated builder is square only")
+    return build_gated_gemm(N, cfg, **hooks)
+  return build_gemm_ws(N, cfg, M, K, **hooks)
+
+
+# Extra tile shapes tried per problem shape by the sweep (BN=192 lets e.g. 3072 divide evenly over the CTAs).
+SWEEP = {
+  "tma_store": LADDER["tma_store"],
+  "hilbert": LADDER["hilbert"],
+  "tma_store_n192": WSCfg(BN=192, tma_store=True),
+  "hilbert_n192": WSCfg(BN=192, tma_store=True, hilbert=True),
+}
+
+# One-off comparisons quoted by the reference (all SMs vs 128 on an H200); here: 128 CTAs vs the device count.
+EXTRA = {
+  "tma_store_132": WSCfg(tma_store=True, num_sm=132),
+  "tma_store_128": WSCfg(tma_store=True, num_sm=128),
+}
