@@ -1,0 +1,347 @@
+"""Benchmark of the B200 bf16 GEMM (the hot path of narain1/tinygrad-hopper-wgmma) — prints ONE JSON line.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload NAME] [--cfg NAME]
+
+Workloads (per rank; one process per GPU, launched by torch.distributed.run for N > 1):
+  gemm4096   (default) M=N=K=4096, the reference's ladder headline. With N GPUs each rank computes its own
+             4096-column shard of a 4096 x 4096N x 4096 GEMM (A replicated, B and C split by columns, no collective in
+             the GEMM): per-GPU work is fixed, scaling "weak".
+  gemm8192   M=N=K=8192 per rank, same sharding.
+  shard32k   M=N=K=32768 split by columns over the N GPUs (32768 x 32768/N x 32768 per rank): scaling "strong".
+A step is one GEMM launch on resident inputs. Between timed steps a 256 MiB buffer is rewritten to flush the 126 MB
+L2, and each step is timed alone with CUDA events on the launching stream; the whole timed region is bracketed by a
+barrier and a synchronize, and the reported time is the max over ranks. Throughput = 2*M*N*K of all ranks / time.
+
+``--impl reference`` times the reference's CPU path instead: its host reference ``a.float() @ b.float()``
+(scripts/smoke.py:41), fp32 accumulate over bf16 inputs plus the bf16 output rounding, on this host's cores
+(the reference's stock tinygrad ``A @ B`` cannot run here). Under torchrun only rank 0 runs it.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path[:0] = [str(ROOT / "tinygrad-hopper-wgmma_b200"), str(ROOT)]
+
+METRIC = "bf16 GEMM TFLOPS at N=4096/8192 (ncu-timed), % of B200 dense peak and of cuBLAS"
+WORKLOADS = {"gemm4096": (4096, 4096, 4096, "weak"), "gemm8192": (8192, 8192, 8192, "weak"),
+             "shard32k": (32768, 32768, 32768, "strong")}
+FLUSH_BYTES = 256 << 20
+CPU_SAMPLE_SECONDS = 10.0
+REFERENCE_BUDGET_S = 90.0
+
+
+def parse_args():
+  ap = argparse.ArgumentParser()
+  ap.add_argument("--gpus", type=int, default=1)
+  ap.add_argument("--steps", type=int, default=2000)
+  ap.add_argument("--warmup", type=int, default=20)
+  ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+  ap.add_argument("--workload", choices=tuple(WORKLOADS), default="gemm4096")
+  ap.add_argument("--cfg", default="best")
+  ap.add_argument("--no-cpu-baseline", action="store_true")
+  ap.add_argument("--no-e2e", action="store_true")
+  return ap.parse_args()
+
+
+def shapes(workload: str, world: int):
+  """(M, n_per_rank, K, N_total, scaling)."""
+  M, N, K, scaling = WORKLOADS[workload]
+  if scaling == "weak": return M, N, K, N * world, scaling
+  if N % world: raise SystemExit(f"{workload}: N={N} does not split over {world} GPUs")
+  return M, N // world, K, N, scaling
+
+
+def measured_peaks() -> dict:
+  p = ROOT / "MEASURED_PEAKS.json"
+  if p.exists(): return {**json.loads(p.read_text()), "source": "measured"}
+  return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+def profiled_traffic(kernel_tag: str, flops_per_launch: float):
+  """DRAM bytes per launch from the committed ncu summary (profiles/*.txt lines 'traffic <tag> <bytes> <flops>'),
+  scaled by the FLOPs processed when the capture ran a different size."""
+  for f in sorted((ROOT / "profiles").glob("*.txt")):
+    for line in f.read_text().splitlines():
+      parts = line.split()
+      if len(parts) == 4 and parts[0] == "traffic" and parts[1] == kernel_tag:
+        return float(parts[2]) * flops_per_launch / float(parts[3])
+  return None
+
+
+# ------------------------------------------------------------------------------------------------------------------
+# clocks during the timed region (NVML reads only; no setting is changed)
+# ------------------------------------------------------------------------------------------------------------------
+class ClockSampler:
+  REASONS = {"gpu_idle": 0x1, "applications_clocks_setting": 0x2, "sw_power_cap": 0x4, "hw_slowdown": 0x8,
+             "sync_boost": 0x10, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40, "hw_power_brake_slowdown": 0x80,
+             "display_clock_setting": 0x100}
+
+  def __init__(self, device_index: int, period_s: float = 0.01):
+    self.samples, self.reasons, self.period, self.ok = [], 0, period_s, False
+    self._stop = threading.Event()
+    try:
+      import pynvml
+      pynvml.nvmlInit()
+      self.nv = pynvml
+      self.h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+      self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+      self.ok = True
+    except Exception as exc:   # NVML missing: report that instead of clocks
+      self.err = repr(exc)
+
+  def _run(self):
+    while not self._stop.is_set():
+      try:
+        self.samples.append(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
+        self.reasons |= self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+      except Exception:
+        pass
+      time.sleep(self.period)
+
+  def __enter__(self):
+    if self.ok:
+      self.t = threading.Thread(target=self._run, daemon=True)
+      self.t.start()
+    return self
+
+  def __exit__(self, *exc):
+    if self.ok:
+      self._stop.set()
+      self.t.join()
+
+  def summary(self) -> dict:
+    if not self.ok: return {"error": self.err}
+    active = [k for k, v in self.REASONS.items() if self.reasons & v and k != "gpu_idle"]
+    return {"sm_mhz": statistics.median(self.samples) if self.samples else None, "sm_max_mhz": self.max_mhz,
+            "samples": len(self.samples), "reasons": active}
+
+
+# ------------------------------------------------------------------------------------------------------------------
+# reference arm: the CPU path
+# ------------------------------------------------------------------------------------------------------------------
+def cpu_gemm_tflops(M: int, N: int, K: int, seconds: float, reps_min: int = 1, reps_max: int | None = None):
+  """Time the oracle's full operator (fp32 accumulate + bf16 rounding) on this host. Returns (tflops, reps, secs)."""
+  from oracle import gemm_ref
+  a_bits, b_bits = gemm_ref.randn_bf16_bits((M, K), 0), gemm_ref.randn_bf16_bits((K, N), 1)
+  a32, b32 = gemm_ref.bf16_bits_to_f32(a_bits), gemm_ref.bf16_bits_to_f32(b_bits)
+  gemm_ref.f32_to_bf16_bits(a32 @ b32)   # warm the BLAS thread pool
+  reps, t0 = 0, time.perf_counter()
+  while reps < reps_min or (time.perf_counter() - t0 < seconds and (reps_max is None or reps < reps_max)):
+    gemm_ref.f32_to_bf16_bits(a32 @ b32)
+    reps += 1
+  dt = time.perf_counter() - t0
+  return 2.0 * M * N * K * reps / dt / 1e12, reps, dt
+
+
+def blas_threads() -> int:
+  try:
+    from threadpoolctl import threadpool_info
+    return max((i.get("num_threads", 1) for i in threadpool_info() if i.get("user_api") == "blas"), default=1)
+  except Exception:
+    return len(os.sched_getaffinity(0))
+
+
+def run_reference(args):
+  if int(os.environ.get("RANK", "0")) != 0: return   # rank 0 alone runs the CPU arm
+  M, n, K, N_total, scaling = shapes(args.workload, 1)
+  from oracle import gemm_ref
+  # One step = the rank-0 GEMM restricted to a sample of cap_M rows, sized so that warm-up + steps take about
+  # REFERENCE_BUDGET_S on this host (the metric is per FLOP, so a row sample measures the same throughput).
+  probe_rows = 256
+  pa, pb = gemm_ref.randn_bf16_bits((probe_rows, K), 2), gemm_ref.randn_bf16_bits((K, n), 3)
+  pa32, pb32 = gemm_ref.bf16_bits_to_f32(pa), gemm_ref.bf16_bits_to_f32(pb)
+  gemm_ref.f32_to_bf16_bits(pa32 @ pb32)
+  t0 = time.perf_counter()
+  gemm_ref.f32_to_bf16_bits(pa32 @ pb32)
+  per_row = (time.perf_counter() - t0) / probe_rows
+  budget_step = REFERENCE_BUDGET_S / max(1, args.steps + args.warmup)
+  cap_M = int(min(M, max(64, budget_step / max(per_row, 1e-9))) // 64 * 64) or 64
+  a_bits, b_bits = gemm_ref.randn_bf16_bits((cap_M, K), 0), gemm_ref.randn_bf16_bits((K, n), 1)
+  a32, b32 = gemm_ref.bf16_bits_to_f32(a_bits), gemm_ref.bf16_bits_to_f32(b_bits)
+  for _ in range(args.warmup): gemm_ref.f32_to_bf16_bits(a32 @ b32)
+  t0 = time.perf_counter()
+  for _ in range(args.steps): gemm_ref.f32_to_bf16_bits(a32 @ b32)
+  dt = time.perf_counter() - t0
+  tflops = 2.0 * cap_M * n * K * args.steps / dt / 1e12
+  cores = blas_threads()
+  sample = f"{args.steps} x numpy fp32 GEMM {cap_M}x{n}x{K} + bf16 rounding (rows capped at {cap_M} of {M})"
+  print(json.dumps({
+    "impl": "reference", "metric": METRIC, "value": round(tflops, 4), "unit": "TFLOPS", "n_gpus": args.gpus,
+    "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 3),
+    "higher_is_better": True, "scaling": scaling, "vs_baseline": None, "dtype": "bf16 in, fp32 accumulate",
+    "data": "synthetic: seeded N(0,1) rounded to bf16",
+    "config": {"workload": args.workload, "M": cap_M, "N": n, "K": K,
+               "path": "reference CPU path stand-in: numpy fp32 matmul of bf16-exact inputs (scripts/smoke.py:41)"},
+    "cpu_baseline": {"value": round(tflops, 4), "unit": "TFLOPS", "cores": cores, "kind": "port", "sample": sample},
+    "e2e": {"value": round(tflops, 4), "unit": "TFLOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    "gpu_launches": 0}), flush=True)
+
+
+# ------------------------------------------------------------------------------------------------------------------
+# our arm
+# ------------------------------------------------------------------------------------------------------------------
+def pick_cfg(name: str):
+  from hopper_wgmma import WSCfg
+  from hopper_wgmma.ladder import LADDER, SWEEP
+  if name == "best": return "best", WSCfg(tma_store=True, cluster=2, hilbert=True)
+  table = {**LADDER, **SWEEP}
+  if name not in table: raise SystemExit(f"unknown --cfg {name}; choose from best, {', '.join(table)}")
+  return name, table[name]
+
+
+def run_ours(args):
+  import torch
+  import torch.distributed as dist
+
+  from hopper_wgmma import shard
+  from hopper_wgmma.gemm import build_gemm_ws
+
+  rank, world = int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1"))
+  local = int(os.environ.get("LOCAL_RANK", "0"))
+  if world != args.gpus: raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+  torch.cuda.set_device(local)
+  dev = torch.device("cuda", local)
+  if world > 1:
+    from datetime import timedelta
+    dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+
+  def barrier():
+    if world > 1: dist.barrier()
+
+  M, n, K, N_total, scaling = shapes(args.workload, world)
+  cfg_name, cfg = pick_cfg(args.cfg)
+  flops_rank = 2.0 * M * n * K
+
+  # inputs resident in HBM: A replicated (same seed everywhere), this rank's K-major B shard, this rank's C shard
+  g = torch.Generator(device=dev).manual_seed(1234)
+  A = torch.randn((M, K), generator=g, device=dev, dtype=torch.float32).to(torch.bfloat16)
+  gb = torch.Generator(device=dev).manual_seed(5678 + rank)
+  BT = torch.randn((n, K), generator=gb, device=dev, dtype=torch.float32).to(torch.bfloat16)
+  C = torch.full((M, n), float("nan"), dtype=torch.bfloat16, device=dev)
+  flush = torch.empty(FLUSH_BYTES // 4, dtype=torch.int32, device=dev)
+  launch = shard.local_gemm(A, BT, C, cfg)
+  info = launch.info()
+
+  def timed(fn, steps):
+    """Per-step device time (ms) with an L2 flush before every step, plus the max over ranks of the total."""
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    barrier()
+    torch.cuda.synchronize()
+    for i in range(steps):
+      flush.zero_()
+      starts[i].record()
+      fn()
+      ends[i].record()
+    torch.cuda.synchronize()
+    barrier()
+    per = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    total = sum(per)
+    if world > 1: total = shard.max_over_ranks(total, device=dev)
+    return total, per
+
+  # correctness gate on the benchmark's own inputs before timing (poisoned C, cuBLAS comparison)
+  launch()
+  launch.check()
+  ref = (A @ BT.t()).float()
+  rel = float((C.float() - ref).abs().max() / (ref.abs().max() + 1e-9))
+  nan = int(torch.isnan(C).sum())
+  del ref
+
+  for _ in range(args.warmup): launch()
+  torch.cuda.synchronize()
+  with ClockSampler(local) as clocks:
+    total_ms, per = timed(launch, args.steps)
+  launch.check()
+  ms = total_ms / args.steps
+  value = flops_rank * world / (ms * 1e-3) / 1e12
+  peaks = measured_peaks()
+  achieved = flops_rank / (statistics.mean(per) * 1e-3) / 1e12
+
+  # cuBLAS on the same inputs, same protocol (the bar the reference compares against)
+  cub_steps = min(args.steps, 200)
+  for _ in range(5): torch.matmul(A, BT.t(), out=C)
+  cub_total, _ = timed(lambda: torch.matmul(A, BT.t(), out=C), cub_steps)
+  cub_tflops = flops_rank * world / (cub_total / cub_steps * 1e-3) / 1e12
+
+  # end to end through the public API: pinned host A and B in, the operator (K-major copy of B, plan, launch), C out
+  e2e = None
+  if not args.no_e2e:
+    hA = torch.empty((M, K), dtype=torch.bfloat16, pin_memory=True)
+    hB = torch.empty((K, n), dtype=torch.bfloat16, pin_memory=True)
+    hC = torch.empty((M, n), dtype=torch.bfloat16, pin_memory=True)
+    hA.copy_(A.cpu())
+    hB.copy_(BT.t().cpu())
+    dA, dB, dC = torch.empty_like(A), torch.empty((K, n), dtype=torch.bfloat16, device=dev), torch.empty_like(C)
+    run = build_gemm_ws(n, cfg, M, K)
+
+    def e2e_step():
+      dA.copy_(hA, non_blocking=True)
+      dB.copy_(hB, non_blocking=True)
+      run(dA, dB, dC)()
+      hC.copy_(dC, non_blocking=True)
+    e2e_steps = max(3, min(args.steps, 30))
+    for _ in range(3): e2e_step()
+    torch.cuda.synchronize()
+    barrier()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for _ in range(e2e_steps): e2e_step()
+    ev1.record()
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = ev0.elapsed_time(ev1)
+    if world > 1: e2e_ms = shard.max_over_ranks(e2e_ms, device=dev)
+    e2e = {"value": round(flops_rank * world / (e2e_ms / e2e_steps * 1e-3) / 1e12, 3), "unit": "TFLOPS",
+           "h2d_bytes_per_step": 2 * (M * K + K * n), "d2h_bytes_per_step": 2 * M * n,
+           "path": "pinned host A,B -> build_gemm_ws(...)(A, B, C)() (K-major copy of B, plan, launch) -> host C",
+           "steps": e2e_steps}
+
+  cpu = None
+  if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    tf, reps, secs = cpu_gemm_tflops(2048, 2048, 2048, CPU_SAMPLE_SECONDS, reps_min=2)
+    cpu = {"value": round(tf, 4), "unit": "TFLOPS", "cores": blas_threads(), "kind": "port",
+           "sample": f"{reps} x numpy fp32 GEMM 2048x2048x2048 + bf16 rounding in {secs:.1f} s"}
+
+  if world > 1:
+    dist.barrier()
+    dist.destroy_process_group()
+  if rank != 0: return
+  tag = f"sm100_gemm_ws_{'pair' if info['paired'] else 'cta'}_{'tmast' if cfg.tma_store else 'reg'}"
+  traffic = profiled_traffic(tag, flops_rank)
+  line = {
+    "metric": METRIC, "value": round(value, 3), "unit": "TFLOPS", "n_gpus": world, "steps": args.steps,
+    "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": True, "scaling": scaling,
+    "vs_baseline": None, "dtype": "bf16", "data": "synthetic: seeded N(0,1) rounded to bf16, resident in HBM",
+    "config": {"workload": args.workload, "M": M, "N": N_total, "K": K, "n_per_gpu": n, "cfg": cfg_name,
+               "cfg_name": cfg.name, "kernel": info["kernel"], "grid": info["grid"], "smem": info["smem_bytes"],
+               "parallelism": f"N-column shards x{world} (A replicated, no collective in the GEMM)",
+               "l2": "flushed between steps (256 MiB write); each step timed alone with CUDA events"},
+    "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                 "frac": round(achieved / peaks["bf16_tflops"], 4), "traffic": traffic,
+                 "peak_source": f"{peaks['source']} bf16_tflops (burst, cuBLAS 8192^3)",
+                 "algorithmic_flops_per_launch": flops_rank},
+    "cublas": {"value": round(cub_tflops, 3), "unit": "TFLOPS", "ours_over_cublas": round(value / cub_tflops, 4),
+               "steps": cub_steps},
+    "parity": {"rel_err_vs_cublas": rel, "nan_after_poison": nan},
+    "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": args.steps, "clocks": clocks.summary(),
+  }
+  print(json.dumps(line), flush=True)
+
+
+def main():
+  args = parse_args()
+  if args.impl == "reference": run_reference(args)
+  else: run_ours(args)
+
+
+if __name__ == "__main__":
+  main()

@@ -51,6 +51,9 @@ enum {
  *   hilbert     1 = Hilbert tile order dealt round-robin over the clusters (gemm.py:218-240), ragged allowed
  *   acc_bufs    accumulator buffers in tensor memory: 0 = auto (2 when 2 * BN <= 512), 1 or 2
  *   wait_budget_ns  per-wait device time limit; 0 = 4 s
+ *   n_mma       tcgen05.mma instructions along N per K step (1 or 2; persistent kernel only): a tile is n_mma * BN
+ *               columns wide, so n_mma = 2 with BN = 256 gives 128 x 512 per CTA (256 x 512 per CTA pair), which
+ *               reads 25% fewer operand bytes per FLOP than 256 x 256 at the cost of a single TMEM accumulator
  *   debug_skip_job  test hook: the producer never loads this job (-1 = off) so that the kernel's waits run out and
  *                   the launch reports an error instead of hanging
  */
@@ -69,7 +72,7 @@ typedef struct bg_cfg {
   int32_t acc_bufs;
   int64_t wait_budget_ns;
   int32_t debug_skip_job;
-  int32_t reserved;
+  int32_t n_mma;
 } bg_cfg;
 
 /* What a plan resolved to (for reports and tests). */

@@ -108,13 +108,18 @@ def _b200_cases():
     ("consumer1_tmast_bn64", WSCfg(consumers=1, BN=64, tma_store=True), (320, 192, 128)),
     ("tall_k", WSCfg(BN=128, tma_store=True, cluster=2), (256, 256, 4096)),
     ("many_tiles_pair", WSCfg(tma_store=True, cluster=2, hilbert=True), (2048, 2048, 512)),
+    ("pair_wide", WSCfg(tma_store=True, cluster=2, n_mma=2), (512, 1024, 256)),
+    ("wide_cta_regstore", WSCfg(BN=128, n_mma=2), (256, 512, 128)),
+    ("wide_pair_hilbert_ragged", WSCfg(BN=128, n_mma=2, cluster=2, tma_store=True, hilbert=True, num_sm=6),
+     (768, 1280, 192)),
+    ("wide_c1_bn80", WSCfg(BN=80, n_mma=2, consumers=1), (128, 320, 64)),
     ("gated_c1", GatedCfg(consumers=1, BN=128), (512, 512, 512)),
     ("ring_bn256", GatedCfg(consumers=0, BN=256, stages=2), (256, 256, 256)),
     ("ring_bn64", GatedCfg(consumers=0, BN=64, stages=3), (192, 192, 192)),
   ]
 
 
-@pytest.mark.parametrize("idx", range(19))
+@pytest.mark.parametrize("idx", range(23))
 def test_b200_cases(idx, cuda_dev):
   from hopper_wgmma.ladder import build
   name, cfg, (M, N, K) = _b200_cases()[idx]

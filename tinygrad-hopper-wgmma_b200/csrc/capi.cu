@@ -10,6 +10,8 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <array>
+#include <map>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -134,12 +136,18 @@ void grouped_order(int mt, int nt, int gm, int gn, std::vector<int32_t>& out) {
 using WsKernel = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const GemmParams);
 using RingKernel = void (*)(const CUtensorMap, const CUtensorMap, const GemmParams);
 
-WsKernel pick_ws(int bm, bool paired, bool tma_store) {
+template <int NB>
+WsKernel pick_ws_nb(int bm, bool paired, bool tma_store) {
+  using namespace sm100;
   if (bm == 128) {
-    if (paired) return tma_store ? sm100::sm100_gemm_ws<128, true, true> : sm100::sm100_gemm_ws<128, true, false>;
-    return tma_store ? sm100::sm100_gemm_ws<128, false, true> : sm100::sm100_gemm_ws<128, false, false>;
+    if (paired) return tma_store ? sm100_gemm_ws<128, true, true, NB> : sm100_gemm_ws<128, true, false, NB>;
+    return tma_store ? sm100_gemm_ws<128, false, true, NB> : sm100_gemm_ws<128, false, false, NB>;
   }
-  return tma_store ? sm100::sm100_gemm_ws<64, false, true> : sm100::sm100_gemm_ws<64, false, false>;
+  return tma_store ? sm100_gemm_ws<64, false, true, NB> : sm100_gemm_ws<64, false, false, NB>;
+}
+
+WsKernel pick_ws(int bm, bool paired, bool tma_store, int nblk) {
+  return nblk == 2 ? pick_ws_nb<2>(bm, paired, tma_store) : pick_ws_nb<1>(bm, paired, tma_store);
 }
 
 RingKernel pick_ring(int bm) { return bm == 128 ? sm100::sm100_gemm_ring<128> : sm100::sm100_gemm_ring<64>; }
@@ -198,12 +206,66 @@ struct DeviceGuard {
   }
 };
 
+// Device storage shared by the plans of one device, so that building a plan allocates nothing once warm (no
+// cudaMalloc / cudaFree, which can synchronize the device, on the path of a caller that plans per batch):
+//   * tile tables, one per distinct schedule, uploaded on first use and kept for the life of the process;
+//   * error words, one per live plan, handed out from 4 KiB slabs and returned when the plan is destroyed.
+struct DeviceStore {
+  std::mutex mu;
+  std::map<std::array<int, 6>, int32_t*> tables;
+  std::vector<unsigned int*> free_words;
+};
+
+DeviceStore& device_store(int dev) {
+  static DeviceStore stores[64];
+  return stores[dev & 63];
+}
+
+int32_t store_table(int dev, const std::array<int, 6>& key, const std::vector<int32_t>& host, int32_t** out) {
+  DeviceStore& s = device_store(dev);
+  std::lock_guard<std::mutex> lock(s.mu);
+  auto it = s.tables.find(key);
+  if (it != s.tables.end()) {
+    *out = it->second;
+    return 0;
+  }
+  int32_t* d = nullptr;
+  cudaError_t e = cudaMalloc(&d, host.size() * sizeof(int32_t));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(tile table)");
+  e = cudaMemcpy(d, host.data(), host.size() * sizeof(int32_t), cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) {
+    cudaFree(d);
+    return cuda_fail(e, "cudaMemcpy(tile table)");
+  }
+  s.tables.emplace(key, d);
+  *out = d;
+  return 0;
+}
+
+int32_t take_error_word(int dev, unsigned int** out) {
+  DeviceStore& s = device_store(dev);
+  std::lock_guard<std::mutex> lock(s.mu);
+  if (s.free_words.empty()) {
+    constexpr int kWords = 1024;
+    unsigned int* slab = nullptr;
+    cudaError_t e = cudaMalloc(&slab, kWords * sizeof(unsigned int));
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(error words)");
+    for (int i = kWords - 1; i >= 0; --i) s.free_words.push_back(slab + i);
+  }
+  unsigned int* w = s.free_words.back();
+  cudaError_t e = cudaMemset(w, 0, sizeof(unsigned int));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemset(error word)");
+  s.free_words.pop_back();
+  *out = w;
+  return 0;
+}
+
 void free_plan(bg_plan* p) {
   if (p == nullptr) return;
-  {
-    DeviceGuard g(p->device);
-    if (p->d_sched) cudaFree(p->d_sched);
-    if (p->d_err) cudaFree(p->d_err);
+  if (p->d_err) {
+    DeviceStore& s = device_store(p->device);
+    std::lock_guard<std::mutex> lock(s.mu);
+    s.free_words.push_back(p->d_err);
   }
   delete p;
 }
@@ -301,14 +363,17 @@ int32_t bg_plan_create(bg_plan** out, const bg_cfg* cfg, int64_t M, int64_t N, i
   const int cl = c.cluster;
   const bool paired = c.kind == BG_KIND_WS && cl == 2 && bm == 128;
   const int bn = c.BN;
+  const int nblk = c.n_mma == 0 ? 1 : c.n_mma;
+  if (nblk < 1 || nblk > 2 || (nblk > 1 && c.kind != BG_KIND_WS)) return fail(-1, "n_mma must be 1 or 2 (persistent kernel)");
+  const int width = bn * nblk;   // output columns per tile
   const int bn_local = paired ? bn / 2 : bn;
 
   // ---- shape contract (gemm.py:300-311)
   if (M <= 0 || N <= 0 || K <= 0) return fail(-1, "M, N and K must be positive");
-  if (M % bm || N % bn || K % 64)
+  if (M % bm || N % width || K % 64)
     return fail(-1, "shape %lldx%lldx%lld not a multiple of tile %dx%dx64", (long long)M, (long long)N, (long long)K, bm,
-                bn);
-  const int64_t mt = M / bm, nt = N / bn, nkb = K / 64;
+                width);
+  const int64_t mt = M / bm, nt = N / width, nkb = K / 64;
   if (mt % cl) return fail(-1, "%lld row tiles not divisible by cluster %d", (long long)mt, cl);
   const int64_t cmt = mt / cl;
   if (cmt > 0xFFFF || nt > 0xFFFF || cmt * nt > (1ll << 30) || nkb > (1ll << 30))
@@ -327,7 +392,8 @@ int32_t bg_plan_create(bg_plan** out, const bg_cfg* cfg, int64_t M, int64_t N, i
 
   // ---- shared memory: [A stages][B stages][C staging][barriers], +1024 bytes to align the base
   const uint32_t a_stage = static_cast<uint32_t>(bm) * 128u;
-  const uint32_t b_stage = static_cast<uint32_t>(bn_local) * 128u;
+  const uint32_t b_block = static_cast<uint32_t>(bn_local) * 128u;
+  const uint32_t b_stage = b_block * static_cast<uint32_t>(nblk);
   const uint32_t c_bytes = c.tma_store ? static_cast<uint32_t>(bm) * 256u : 0u;
   const uint32_t fixed = 1024u + c_bytes + (c.kind == BG_KIND_RING ? 16u : 48u);
   int stages = c.stages;
@@ -343,8 +409,8 @@ int32_t bg_plan_create(bg_plan** out, const bg_cfg* cfg, int64_t M, int64_t N, i
   // ---- accumulators in tensor memory
   int acc_bufs = c.acc_bufs;
   if (c.kind != BG_KIND_WS) acc_bufs = 1;
-  if (acc_bufs == 0) acc_bufs = 2 * bn <= 512 ? 2 : 1;
-  if (acc_bufs * bn > 512) return fail(-1, "%d accumulators of %d columns exceed tensor memory", acc_bufs, bn);
+  if (acc_bufs == 0) acc_bufs = 2 * width <= 512 ? 2 : 1;
+  if (acc_bufs * width > 512) return fail(-1, "%d accumulators of %d columns exceed tensor memory", acc_bufs, width);
 
   std::unique_ptr<bg_plan, void (*)(bg_plan*)> p(new bg_plan, free_plan);
   p->device = device;
@@ -363,14 +429,17 @@ int32_t bg_plan_create(bg_plan** out, const bg_cfg* cfg, int64_t M, int64_t N, i
   const int64_t tiles = cmt * nt;
   int64_t nclusters = tiles;
   std::vector<int32_t> sched;
+  std::array<int, 6> sched_key{};
   if (c.kind == BG_KIND_WS) {
     const int num_sm = c.num_sm > 0 ? c.num_sm : sm_count;
     nclusters = std::min<int64_t>(num_sm / cl, tiles);
     if (c.hilbert) {
+      sched_key = {device, 1, static_cast<int>(cmt), static_cast<int>(nt), 0, 0};
       hilbert_order(static_cast<int>(cmt), static_cast<int>(nt), sched);
     } else {
       const int gm = std::min<int>(std::max(c.group_m / cl, 1), static_cast<int>(cmt));
       const int gn = std::min<int>(c.group_n, static_cast<int>(nt));
+      sched_key = {device, 0, static_cast<int>(cmt), static_cast<int>(nt), gm, gn};
       grouped_order(static_cast<int>(cmt), static_cast<int>(nt), gm, gn, sched);
     }
   }
@@ -381,7 +450,7 @@ int32_t bg_plan_create(bg_plan** out, const bg_cfg* cfg, int64_t M, int64_t N, i
     p->ring = pick_ring(bm);
     fn = reinterpret_cast<const void*>(p->ring);
   } else {
-    p->ws = pick_ws(bm, paired, p->tma_store);
+    p->ws = pick_ws(bm, paired, p->tma_store, nblk);
     fn = reinterpret_cast<const void*>(p->ws);
   }
   cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_optin);
@@ -390,7 +459,7 @@ int32_t bg_plan_create(bg_plan** out, const bg_cfg* cfg, int64_t M, int64_t N, i
   // in tcgen05.alloc behind another (and CTA pairs waiting on each other could deadlock). Pad the shared-memory
   // request until the occupancy limit keeps co-resident CTAs within the SM's tensor memory.
   {
-    const int tcols = static_cast<int>(pow2_cols(acc_bufs * bn));
+    const int tcols = static_cast<int>(pow2_cols(acc_bufs * width));
     const int allowed = 512 / tcols;
     for (;;) {
       int blocks = 0;
@@ -435,17 +504,13 @@ int32_t bg_plan_create(bg_plan** out, const bg_cfg* cfg, int64_t M, int64_t N, i
   }
 
   // ---- device buffers: tile table and error word
-  if (!sched.empty()) {
-    if ((e = cudaMalloc(&p->d_sched, sched.size() * sizeof(int32_t))) != cudaSuccess) return cuda_fail(e, "cudaMalloc");
-    if ((e = cudaMemcpy(p->d_sched, sched.data(), sched.size() * sizeof(int32_t), cudaMemcpyHostToDevice)) != cudaSuccess)
-      return cuda_fail(e, "cudaMemcpy(tile table)");
-  }
-  if ((e = cudaMalloc(&p->d_err, 256)) != cudaSuccess) return cuda_fail(e, "cudaMalloc");
-  if ((e = cudaMemset(p->d_err, 0, 256)) != cudaSuccess) return cuda_fail(e, "cudaMemset");
+  if (!sched.empty() && (st = store_table(device, sched_key, sched, &p->d_sched))) return st;
+  if ((st = take_error_word(device, &p->d_err))) return st;
 
   GemmParams& kp = p->kp;
   kp.num_kb = static_cast<int>(nkb);
   kp.bn = bn;
+  kp.nblk = nblk;
   kp.bn_local = bn_local;
   kp.stages = stages;
   kp.tiles = static_cast<int>(tiles);
@@ -453,11 +518,12 @@ int32_t bg_plan_create(bg_plan** out, const bg_cfg* cfg, int64_t M, int64_t N, i
   kp.cl = c.kind == BG_KIND_RING ? 1 : cl;
   kp.nt = static_cast<int>(nt);
   kp.acc_bufs = acc_bufs;
-  kp.acc_stride = bn;
-  kp.tmem_cols = pow2_cols(acc_bufs * bn);
+  kp.acc_stride = width;
+  kp.tmem_cols = pow2_cols(acc_bufs * width);
   kp.idesc = make_idesc(paired ? 2 * bm : bm, bn);
   kp.tx_bytes = (a_stage + b_stage) * (paired ? 2u : 1u);
   kp.a_stage_bytes = a_stage;
+  kp.b_block_bytes = b_block;
   kp.b_stage_bytes = b_stage;
   kp.sched = p->d_sched;
   kp.C = static_cast<__nv_bfloat16*>(C);
@@ -466,9 +532,9 @@ int32_t bg_plan_create(bg_plan** out, const bg_cfg* cfg, int64_t M, int64_t N, i
   kp.budget_ns = c.wait_budget_ns > 0 ? static_cast<unsigned long long>(c.wait_budget_ns) : 4000000000ull;
   kp.skip_job = c.debug_skip_job;
 
-  snprintf(p->name, sizeof(p->name), "%s<BM=%d,%s,%s> BN=%d stages=%d acc=%d", c.kind == BG_KIND_RING ? "sm100_gemm_ring" : "sm100_gemm_ws",
-           bm, paired ? "pair" : (cl == 2 ? "cluster2" : "cta"), p->tma_store ? "tma_store" : "reg_store", bn, stages,
-           acc_bufs);
+  snprintf(p->name, sizeof(p->name), "%s<BM=%d,%s,%s> BN=%dx%d stages=%d acc=%d", c.kind == BG_KIND_RING ? "sm100_gemm_ring" : "sm100_gemm_ws",
+           bm, paired ? "pair" : (cl == 2 ? "cluster2" : "cta"), p->tma_store ? "tma_store" : "reg_store", bn, nblk,
+           stages, acc_bufs);
   *out = p.release();
   return 0;
 }

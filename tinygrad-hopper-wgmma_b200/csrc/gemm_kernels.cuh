@@ -45,8 +45,9 @@ enum : uint32_t {
 
 struct GemmParams {
   int num_kb;              // K / 64
-  int bn;                  // MMA N: output columns per tile (the whole pair's tile when PAIRED)
-  int bn_local;            // rows of BT this CTA loads per stage (bn / 2 when PAIRED)
+  int bn;                  // MMA N: columns per tcgen05.mma (the whole pair's when PAIRED)
+  int nblk;                // MMAs along N per K step: a tile is nblk * bn columns wide (1 or 2)
+  int bn_local;            // rows of BT this CTA loads per N block and stage (bn / 2 when PAIRED)
   int stages;              // shared-memory ring depth
   int tiles;               // schedule entries (cluster tiles)
   int nclusters;           // clusters (persistent workers) in the grid
@@ -58,7 +59,8 @@ struct GemmParams {
   uint32_t idesc;          // tcgen05 instruction descriptor (bf16 x bf16 -> f32, K-major, M, N)
   uint32_t tx_bytes;       // bytes that complete one stage's FULL barrier (both CTAs' loads when PAIRED)
   uint32_t a_stage_bytes;  // BM * 128
-  uint32_t b_stage_bytes;  // bn_local * 128
+  uint32_t b_block_bytes;  // bn_local * 128: one N block of B in a stage
+  uint32_t b_stage_bytes;  // nblk * b_block_bytes
   const int32_t* sched;    // [tiles] entries (cluster row tile << 16) | column tile; entry i runs on cluster
                            // i % nclusters as that cluster's (i / nclusters)-th tile
   __nv_bfloat16* C;        // output base (register epilogue)
@@ -110,7 +112,7 @@ __device__ __forceinline__ void epilogue_registers(uint32_t tacc, __nv_bfloat16*
   }
 }
 
-template <int BM, bool PAIRED, bool TMA_STORE>
+template <int BM, bool PAIRED, bool TMA_STORE, int NB>
 __global__ void __launch_bounds__(kWsThreads, 1)
     sm100_gemm_ws(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                   const __grid_constant__ CUtensorMap tmC, const GemmParams p) {
@@ -170,101 +172,119 @@ __global__ void __launch_bounds__(kWsThreads, 1)
   const uint32_t tmem_base = *tslot_ptr;
 
   if (warp == 0) {
-    // ------------------------------------------------------------------ TMA producer
-    if (lane == 0) {
-      uint32_t stage = 0, phase = 0;
-      int job = 0;
-      bool failed = false;
-      for (int i = 0; !failed; ++i) {
-        const int idx = cid + i * p.nclusters;
-        if (idx >= p.tiles) break;
-        int cm, tn;
-        tile_coords(p, idx, cm, tn);
-        const int row_a = (cm * p.cl + static_cast<int>(rank)) * BM;
-        const int row_b = tn * p.bn + (PAIRED ? static_cast<int>(rank) * p.bn_local : 0);
-        for (int kb = 0; kb < p.num_kb; ++kb, ++job) {
-          if (!mbar_wait_bounded(empty0 + 8u * stage, phase ^ 1u, budget)) {
-            record_error(p.err, kErrProducer, job);
-            failed = true;
-            break;
+    // ------------------------------------------------------------------ TMA producer (one elected lane issues)
+    uint32_t stage = 0, phase = 0;
+    int job = 0;
+    bool failed = false;
+    for (int i = 0; !failed; ++i) {
+      const int idx = cid + i * p.nclusters;
+      if (idx >= p.tiles) break;
+      int cm, tn;
+      tile_coords(p, idx, cm, tn);
+      const int row_a = (cm * p.cl + static_cast<int>(rank)) * BM;
+      const int row_b = tn * p.bn * NB + (PAIRED ? static_cast<int>(rank) * p.bn_local : 0);
+      for (int kb = 0; kb < p.num_kb; ++kb, ++job) {
+        if (!mbar_wait_warp(empty0 + 8u * stage, phase ^ 1u, budget)) {
+          if (lane == 0) record_error(p.err, kErrProducer, job);
+          failed = true;
+          break;
+        }
+        if (job != p.skip_job && elect_one()) {
+          const uint32_t fb = full0 + 8u * stage;
+          const uint32_t a_dst = sA + stage * p.a_stage_bytes;
+          const uint32_t b_dst = sB + stage * p.b_stage_bytes;
+          if (PAIRED) {
+            const uint32_t fb_leader = mapa_shared(fb, 0);
+            if (leader) mbar_arrive_expect_tx(fb, p.tx_bytes);
+            tma_load_2d_pair(a_dst, &tmA, fb_leader, kb * kBK, row_a);
+#pragma unroll
+            for (int nb = 0; nb < NB; ++nb)
+              tma_load_2d_pair(b_dst + nb * p.b_block_bytes, &tmB, fb_leader, kb * kBK, row_b + nb * p.bn);
+          } else {
+            mbar_arrive_expect_tx(fb, p.tx_bytes);
+            tma_load_2d(a_dst, &tmA, fb, kb * kBK, row_a);
+#pragma unroll
+            for (int nb = 0; nb < NB; ++nb)
+              tma_load_2d(b_dst + nb * p.b_block_bytes, &tmB, fb, kb * kBK, row_b + nb * p.bn);
           }
-          if (job != p.skip_job) {
-            const uint32_t fb = full0 + 8u * stage;
-            if (PAIRED) {
-              const uint32_t fb_leader = mapa_shared(fb, 0);
-              if (leader) mbar_arrive_expect_tx(fb, p.tx_bytes);
-              tma_load_2d_pair(sA + stage * p.a_stage_bytes, &tmA, fb_leader, kb * kBK, row_a);
-              tma_load_2d_pair(sB + stage * p.b_stage_bytes, &tmB, fb_leader, kb * kBK, row_b);
-            } else {
-              mbar_arrive_expect_tx(fb, p.tx_bytes);
-              tma_load_2d(sA + stage * p.a_stage_bytes, &tmA, fb, kb * kBK, row_a);
-              tma_load_2d(sB + stage * p.b_stage_bytes, &tmB, fb, kb * kBK, row_b);
-            }
-          }
-          if (++stage == static_cast<uint32_t>(p.stages)) {
-            stage = 0;
-            phase ^= 1u;
-          }
+        }
+        __syncwarp();
+        if (++stage == static_cast<uint32_t>(p.stages)) {
+          stage = 0;
+          phase ^= 1u;
         }
       }
-      if (leader) {
-        // Let the loads already issued land before shared memory goes away: the newest job of every stage. On the
-        // normal path the MMA has consumed them all and these waits return at once; after an error elsewhere they
-        // keep the CTA alive until its own copies have arrived. (A pair's FULL barriers live in the even CTA and
-        // count both CTAs' bytes; the odd CTA leaves only after the cluster barrier below.)
-        const int first = job - p.stages < 0 ? 0 : job - p.stages;
-        for (int j = first; j < job; ++j) {
-          if (j == p.skip_job) continue;
-          const uint32_t s = static_cast<uint32_t>(j % p.stages), ph = static_cast<uint32_t>((j / p.stages) & 1);
-          if (!mbar_wait_bounded(full0 + 8u * s, ph, budget)) record_error(p.err, kErrLoadDrain, j);
-        }
+    }
+    if (leader) {
+      // Let the loads already issued land before shared memory goes away: the newest job of every stage. On the
+      // normal path the MMA has consumed them all and these waits return at once; after an error elsewhere they
+      // keep the CTA alive until its own copies have arrived. (A pair's FULL barriers live in the even CTA and
+      // count both CTAs' bytes; the odd CTA leaves only after the cluster barrier below.)
+      const int first = job - p.stages < 0 ? 0 : job - p.stages;
+      for (int j = first; j < job; ++j) {
+        if (j == p.skip_job) continue;
+        const uint32_t s = static_cast<uint32_t>(j % p.stages), ph = static_cast<uint32_t>((j / p.stages) & 1);
+        if (!mbar_wait_warp(full0 + 8u * s, ph, budget) && lane == 0) record_error(p.err, kErrLoadDrain, j);
       }
     }
     __syncwarp();
   } else if (warp == 1) {
-    // ------------------------------------------------------------------ MMA issuer
-    if (lane == 0 && leader) {
+    // ------------------------------------------------------------------ MMA issuer (whole warp, one elected lane)
+    if (leader) {
       uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
       int job = 0;
       bool failed = false;
       for (int i = 0; !failed; ++i) {
         const int idx = cid + i * p.nclusters;
         if (idx >= p.tiles) break;
-        if (!mbar_wait_bounded(tempty0 + 8u * acc, acc_phase ^ 1u, budget)) {
-          record_error(p.err, kErrMmaAcc, i);
+        if (!mbar_wait_warp(tempty0 + 8u * acc, acc_phase ^ 1u, budget)) {
+          if (lane == 0) record_error(p.err, kErrMmaAcc, i);
           break;
         }
         tc_fence_after();
         const uint32_t d = tmem_base + acc * static_cast<uint32_t>(p.acc_stride);
         for (int kb = 0; kb < p.num_kb; ++kb, ++job) {
-          if (!mbar_wait_bounded(full0 + 8u * stage, phase, budget)) {
-            record_error(p.err, kErrMmaFull, job);
+          if (!mbar_wait_warp(full0 + 8u * stage, phase, budget)) {
+            if (lane == 0) record_error(p.err, kErrMmaFull, job);
             failed = true;
             break;
           }
           tc_fence_after();
-          const uint64_t ad = smem_desc_sw128(sA + stage * p.a_stage_bytes);
-          const uint64_t bd = smem_desc_sw128(sB + stage * p.b_stage_bytes);
+          if (elect_one()) {
+            const uint64_t ad = smem_desc_sw128(sA + stage * p.a_stage_bytes);
+            const uint64_t bd = smem_desc_sw128(sB + stage * p.b_stage_bytes);
+            // +32 bytes along K inside the swizzle row = +2 in the descriptor's address field; N block nb reads the
+            // nb-th B sub-tile and accumulates into TMEM columns [nb * bn, (nb + 1) * bn)
 #pragma unroll
-          for (int k = 0; k < kBK / 16; ++k)   // +32 bytes along K inside the swizzle row = +2 in the address field
-            mma_bf16<CG>(d, ad + 2u * k, bd + 2u * k, p.idesc, (kb | k) != 0 ? 1u : 0u);
-          mma_commit<CG>(empty0 + 8u * stage);
-          if (PAIRED) mma_commit<CG>(mapa_shared(empty0 + 8u * stage, 1));
+            for (int k = 0; k < kBK / 16; ++k)
+#pragma unroll
+              for (int nb = 0; nb < NB; ++nb)
+                mma_bf16<CG>(d + static_cast<uint32_t>(nb * p.bn), ad + 2u * k,
+                             bd + static_cast<uint64_t>((nb * p.b_block_bytes) >> 4) + 2u * k, p.idesc,
+                             (kb | k) != 0 ? 1u : 0u);
+            mma_commit<CG>(empty0 + 8u * stage);
+            if (PAIRED) mma_commit<CG>(mapa_shared(empty0 + 8u * stage, 1));
+          }
+          __syncwarp();
           if (++stage == static_cast<uint32_t>(p.stages)) {
             stage = 0;
             phase ^= 1u;
           }
         }
         if (failed) break;
-        mma_commit<CG>(tfull0 + 8u * acc);
-        if (PAIRED) mma_commit<CG>(mapa_shared(tfull0 + 8u * acc, 1));
+        if (elect_one()) {
+          mma_commit<CG>(tfull0 + 8u * acc);
+          if (PAIRED) mma_commit<CG>(mapa_shared(tfull0 + 8u * acc, 1));
+        }
+        __syncwarp();
         if (++acc == static_cast<uint32_t>(p.acc_bufs)) {
           acc = 0;
           acc_phase ^= 1u;
         }
       }
-      mma_commit<CG>(drain);   // every MMA issued above has finished once this arrives
-      if (!mbar_wait_bounded(drain, 0, budget)) record_error(p.err, kErrDrain, 0);
+      if (elect_one()) mma_commit<CG>(drain);   // every MMA issued above has finished once this arrives
+      __syncwarp();
+      if (!mbar_wait_warp(drain, 0, budget) && lane == 0) record_error(p.err, kErrDrain, 0);
     }
     __syncwarp();
   } else if (warp >= 4) {
@@ -279,15 +299,16 @@ __global__ void __launch_bounds__(kWsThreads, 1)
       int cm, tn;
       tile_coords(p, idx, cm, tn);
       const int row0 = (cm * p.cl + static_cast<int>(rank)) * BM + q * ROWS_W;   // first row of this warp
-      const int col0 = tn * p.bn;
-      if (!mbar_wait_bounded(tfull0 + 8u * acc, acc_phase, budget)) {
+      const int width = p.bn * NB;   // output columns of this tile
+      const int col0 = tn * width;
+      if (!mbar_wait_warp(tfull0 + 8u * acc, acc_phase, budget)) {
         record_error(p.err, kErrEpilogue, i);
         break;
       }
       tc_fence_after();
       const uint32_t tacc = tmem_base + lane_base + acc * static_cast<uint32_t>(p.acc_stride);
       if constexpr (TMA_STORE) {
-        const int nchunks = p.bn >> 6;
+        const int nchunks = width >> 6;
 #pragma unroll 1
         for (int c = 0; c < nchunks; ++c, ++chunk) {
           uint32_t v0[32], v1[32];
@@ -321,7 +342,7 @@ __global__ void __launch_bounds__(kWsThreads, 1)
         }
       } else {
         __nv_bfloat16* crow = p.C + static_cast<long long>(row0 + lane) * p.ldc + col0;
-        epilogue_registers(tacc, crow, p.bn, lane < ROWS_W);
+        epilogue_registers(tacc, crow, width, lane < ROWS_W);
       }
       tc_fence_before();
       __syncwarp();

@@ -39,6 +39,16 @@ __device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
   return r;
 }
 
+// One lane of the (fully active) warp returns true: the warp stays converged around single-thread work such as
+// TMA and MMA issue, so the values feeding those instructions remain warp-uniform.
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred = 0;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\telect.sync _|p, 0xffffffff;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(pred));
+  return pred != 0;
+}
+
 __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
@@ -93,6 +103,13 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
       if (mbar_try_wait(bar, parity)) return true;
     if (globaltimer_ns() - t0 > budget_ns) return false;
   }
+}
+
+// Warp-wide bounded wait: every lane waits, then the warp agrees on the outcome, so that a timeout that some lanes
+// see a moment before others cannot split the warp ahead of .sync.aligned instructions.
+__device__ __forceinline__ bool mbar_wait_warp(uint32_t bar, uint32_t parity, uint64_t budget_ns) {
+  const bool ok = mbar_wait_bounded(bar, parity, budget_ns);
+  return __all_sync(0xffffffffu, ok);
 }
 
 // ---------------------------------------------------------------------------------------------------------------

@@ -140,7 +140,8 @@ class WSCfg:
   regs: tuple[int, int] | None = None   # register split (producer, consumer); validated, see DESIGN notes
   cluster: int = 1             # 2: two CTAs share one M = 256 MMA (cta_group::2), each loading half of B
   hilbert: bool = False        # Hilbert tile order from a host-built table
-  acc_bufs: int | None = None  # accumulator buffers in tensor memory; None = 2 when 2 * BN <= 512 columns
+  acc_bufs: int | None = None  # accumulator buffers in tensor memory; None = 2 when 2 * width <= 512 columns
+  n_mma: int = 1               # tcgen05.mma instructions along N per K step: tiles are n_mma * BN columns wide
 
   def __post_init__(self):
     if self.BK != 64: raise ValueError("BK must be 64 (one 128-byte swizzle atom)")
@@ -153,23 +154,26 @@ class WSCfg:
     if self.group_m < 1 or self.group_n < 1: raise ValueError("group_m and group_n must be positive")
     if self.regs is not None and (len(self.regs) != 2 or any(r % 8 or not 24 <= r <= 256 for r in self.regs)):
       raise ValueError("regs must be two multiples of 8 in [24, 256]")
+    if self.n_mma not in (1, 2): raise ValueError("n_mma must be 1 or 2")
     if self.acc_bufs is not None and self.acc_bufs not in (1, 2): raise ValueError("acc_bufs must be 1 or 2")
-    if self.acc_bufs == 2 and 2 * self.BN > 512: raise ValueError("two accumulators of BN columns exceed tensor memory")
+    if self.acc_bufs == 2 and 2 * self.width > 512: raise ValueError("two accumulators of the tile width exceed tensor memory")
     if self.stages_used < 2: raise ValueError(f"not even 2 stages fit in {SMEM_LIMIT} bytes of shared memory")
     if self.smem_bytes > SMEM_LIMIT: raise ValueError(f"needs {self.smem_bytes} bytes of shared memory, the limit is {SMEM_LIMIT}")
 
   @property
   def BM(self): return 64 * self.consumers
   @property
+  def width(self): return self.BN * self.n_mma            # output columns per tile
+  @property
   def paired(self): return self.cluster == 2 and self.BM == 128   # cta_group::2 across the CTA pair
   @property
   def threads(self): return 256                         # warp 0 TMA, warp 1 TMEM + MMA, warps 4-7 epilogue
   @property
-  def tmem_cols(self): return self.BN                   # fp32 accumulator columns per buffer (BM lanes)
+  def tmem_cols(self): return self.width                # fp32 accumulator columns per buffer (BM lanes)
   @property
   def a_elems(self): return self.BM * self.BK
   @property
-  def b_elems(self): return (self.BN // 2 if self.paired else self.BN) * self.BK   # this CTA's share of the B tile
+  def b_elems(self): return (self.BN // 2 if self.paired else self.BN) * self.BK * self.n_mma   # this CTA's B share
   @property
   def c_elems(self): return self.BM * 128 if self.tma_store else 0   # 4 warps x 2 buffers x (BM/4 rows x 64 cols)
   @property
@@ -188,14 +192,16 @@ class WSCfg:
     sm = self.num_sm if self.num_sm is not None else "dev"
     return (f"ws_c{self.consumers}_s{st}_n{self.BN}_sm{sm}_g{self.group_m}x{self.group_n}"
             f"{'_tmast' if self.tma_store else ''}{'_hil' if self.hilbert else ''}"
-            f"{f'_r{self.regs[0]}x{self.regs[1]}' if self.regs else ''}{f'_cl{self.cluster}' if self.cluster > 1 else ''}")
+            f"{f'_r{self.regs[0]}x{self.regs[1]}' if self.regs else ''}{f'_cl{self.cluster}' if self.cluster > 1 else ''}"
+            f"{f'_x{self.n_mma}' if self.n_mma > 1 else ''}")
 
   def to_c(self, kind: int = _capi.KIND_WS, num_sm: int | None = None, wait_budget_ns: int = 0,
            debug_skip_job: int = -1) -> _capi.BgCfg:
     return _capi.BgCfg(kind=kind, BN=self.BN, BK=self.BK, stages=self.stages or 0, consumers=self.consumers,
                        num_sm=num_sm or self.num_sm or 0, group_m=self.group_m, group_n=self.group_n,
                        tma_store=int(self.tma_store), cluster=self.cluster, hilbert=int(self.hilbert),
-                       acc_bufs=self.acc_bufs or 0, wait_budget_ns=wait_budget_ns, debug_skip_job=debug_skip_job)
+                       acc_bufs=self.acc_bufs or 0, wait_budget_ns=wait_budget_ns, debug_skip_job=debug_skip_job,
+                       n_mma=self.n_mma)
 
 
 # =============================================================================================================
@@ -239,7 +245,7 @@ def build_gemm_ws(N: int, cfg: WSCfg, M: int | None = None, K: int | None = None
   ``wait_budget_ns`` / ``debug_skip_job`` are test hooks (per-wait time limit; a job the producer never loads)."""
   M, K = N if M is None else M, N if K is None else K
   if min(M, N, K) <= 0: raise ValueError("M, N and K must be positive")
-  BM, BN, BK, CL = cfg.BM, cfg.BN, cfg.BK, cfg.cluster
+  BM, BN, BK, CL = cfg.BM, cfg.width, cfg.BK, cfg.cluster
   if M % BM or N % BN or K % BK: raise ValueError(f"shape {M}x{N}x{K} not a multiple of tile {BM}x{BN}x{BK}")
   MT, NT = M // BM, N // BN
   if MT % CL: raise ValueError(f"{MT} row tiles not divisible by cluster {CL}")

@@ -35,6 +35,15 @@ SWEEP = {
   "hilbert_n192": WSCfg(BN=192, tma_store=True, hilbert=True),
 }
 
+# B200 tile shapes beyond the reference's ladder: CTA pairs with 256 x 512 tiles (two N=256 MMAs per K step, one
+# 512-column TMEM accumulator), which read a quarter fewer operand bytes per FLOP than 256 x 256.
+B200 = {
+  "pair_wide": WSCfg(tma_store=True, cluster=2, n_mma=2),
+  "pair_wide_hilbert": WSCfg(tma_store=True, cluster=2, n_mma=2, hilbert=True),
+  "pair_n128": WSCfg(BN=128, tma_store=True, cluster=2, hilbert=True),
+  "pair_reg": WSCfg(cluster=2, hilbert=True),
+}
+
 # One-off comparisons quoted by the reference (all SMs vs 128 on an H200); here: 128 CTAs vs the device count.
 EXTRA = {
   "tma_store_132": WSCfg(tma_store=True, num_sm=132),

@@ -1,0 +1,112 @@
+"""Launch (and optionally time) GEMM configs on one shape: the reference's measurement workload
+(scripts/ncu_workload.py) for B200.
+
+    python -m hopper_wgmma.workload --shape 4096 --configs tma_store,hilbert --reps 5 --torch --check [--time]
+
+  --shape MxNxK   problem size (or a single N for a square GEMM)
+  --configs a,b   names from ladder.LADDER / SWEEP / EXTRA (or "all"); configs invalid for the shape print SKIP
+  --torch         also launch cuBLAS (torch.matmul) on the same inputs
+  --check         compare each config with cuBLAS once, on NaN-poisoned output, before the timed launches
+  --time          time each config with CUDA events (best and mean of --reps launches, after warm-up) and print
+                  one JSON line per config; without it the script only launches, for Nsight Compute to time
+  --flush         with --time: rewrite a 256 MiB buffer between launches so every launch starts with a cold L2
+
+Output lines: ``CHECK <label> rel=... max|ref|=... ok|MISMATCH``, ``KERNEL <label> <kernel>``, ``SKIP <label>: ...``
+(the reference's formats, scripts/ncu_workload.py:63-69) and, with --time, ``TIME {json}``.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+
+
+def parse_shape(text: str) -> tuple[int, int, int]:
+  dims = [int(x) for x in text.lower().split("x")]
+  if len(dims) == 1: dims *= 3
+  if len(dims) != 3: raise SystemExit(f"bad --shape {text!r}")
+  return dims[0], dims[1], dims[2]
+
+
+def _time(fn, reps: int, warmup: int, flush=None) -> tuple[float, float]:
+  import torch
+  for _ in range(warmup): fn()
+  starts = [torch.cuda.Event(enable_timing=True) for _ in range(reps)]
+  ends = [torch.cuda.Event(enable_timing=True) for _ in range(reps)]
+  torch.cuda.synchronize()
+  for i in range(reps):
+    if flush is not None: flush.zero_()
+    starts[i].record()
+    fn()
+    ends[i].record()
+  torch.cuda.synchronize()
+  us = [s.elapsed_time(e) * 1e3 for s, e in zip(starts, ends)]
+  return min(us), sum(us) / len(us)
+
+
+def main(argv=None) -> int:
+  import torch
+
+  from .ladder import B200, EXTRA, LADDER, SWEEP, build
+  ap = argparse.ArgumentParser()
+  ap.add_argument("--shape", default="4096")
+  ap.add_argument("--configs", default="")
+  ap.add_argument("--reps", type=int, default=5)
+  ap.add_argument("--warmup", type=int, default=3)
+  ap.add_argument("--torch", action="store_true")
+  ap.add_argument("--check", action="store_true")
+  ap.add_argument("--time", action="store_true")
+  ap.add_argument("--flush", action="store_true")
+  args = ap.parse_args(argv)
+  M, N, K = parse_shape(args.shape)
+  table = {**LADDER, **SWEEP, **EXTRA, **B200}
+  names = list(table) if args.configs == "all" else [n for n in args.configs.split(",") if n]
+  dev = torch.device("cuda", torch.cuda.current_device())
+  g = torch.Generator(device=dev).manual_seed(0)
+  a = torch.randn((M, K), generator=g, device=dev).to(torch.bfloat16)
+  b = torch.randn((K, N), generator=g, device=dev).to(torch.bfloat16)
+  c = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+  flush = torch.empty(64 << 20, dtype=torch.int32, device=dev) if args.flush else None
+  flops = 2.0 * M * N * K
+  ref = (a @ b).float() if (args.check or args.torch) else None
+  cub_us = None
+  if args.torch:
+    out = torch.empty_like(c)
+    for _ in range(args.reps): torch.matmul(a, b, out=out)
+    torch.cuda.synchronize()
+    print("KERNEL cublas torch", flush=True)
+    if args.time:
+      best, mean = _time(lambda: torch.matmul(a, b, out=out), args.reps, args.warmup, flush)
+      cub_us = best
+      print("TIME " + json.dumps({"label": "cublas", "shape": [M, N, K], "us_best": round(best, 2),
+                                  "us_mean": round(mean, 2), "tflops": round(flops / best / 1e6, 1)}), flush=True)
+  failed = 0
+  for name in names:
+    cfg = table[name]
+    try:
+      run = build(N, cfg, M, K)
+      launch = run(a, b, c)
+      c.fill_(float("nan"))          # a skipped write can't pass the check
+      launch()
+      launch.check()
+      if args.check:
+        rel = float((c.float() - ref).abs().max() / (ref.abs().max() + 1e-9))
+        bad = not rel <= 4e-3 or bool(torch.isnan(c).any())
+        print(f"CHECK {name} rel={rel:.5f} max|ref|={float(ref.abs().max()):.1f} {'MISMATCH' if bad else 'ok'}",
+              flush=True)
+        failed += bad
+      for _ in range(args.reps): launch()
+      launch.check()
+      print(f"KERNEL {name} {run.kernel_name} {launch.info()['kernel']}", flush=True)
+      if args.time:
+        best, mean = _time(launch, args.reps, args.warmup, flush)
+        rec = {"label": name, "shape": [M, N, K], "kernel": launch.info()["kernel"], "us_best": round(best, 2),
+               "us_mean": round(mean, 2), "tflops": round(flops / best / 1e6, 1)}
+        if cub_us: rec["pct_cublas"] = round(100.0 * cub_us / best, 1)
+        print("TIME " + json.dumps(rec), flush=True)
+    except ValueError as exc:
+      print(f"SKIP {name}: {exc}", flush=True)
+  return 1 if failed else 0
+
+
+if __name__ == "__main__":
+  raise SystemExit(main())
