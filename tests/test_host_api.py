@@ -1,0 +1,230 @@
+"""Host-side parity with the reference's operator API (no GPU needed): the C ABI library loads and exports what the
+header declares; configs, shape contracts, tile orders, ladder tables and helper contracts match what the reference's
+own code returns or raises (tests/golden/reference_host.json, made by tests/golden/make_golden.py)."""
+from __future__ import annotations
+
+import re
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parent.parent
+SMEM_MSG = "needs "
+
+
+# ----------------------------------------------------------------------------------------------------------------
+# the C ABI library
+# ----------------------------------------------------------------------------------------------------------------
+def header_functions() -> set[str]:
+  text = (ROOT / "include" / "sm100_gemm.h").read_text()
+  text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+  return set(re.findall(r"\b(bg_[a-z0-9_]+)\s*\(", text))
+
+
+def test_library_loads_and_exports_every_declared_symbol():
+  from hopper_wgmma import _capi
+  declared = header_functions()
+  assert declared, "no declarations parsed from include/sm100_gemm.h"
+  missing = [name for name in sorted(declared) if not hasattr(_capi.LIB, name)]
+  assert not missing, f"library lacks {missing}"
+  assert set(_capi.EXPORTS) <= declared
+  assert _capi.LIB.bg_version() >= 100
+
+
+def test_library_reports_missing_device_as_runtime_error_not_crash():
+  import torch
+  if torch.cuda.is_available(): pytest.skip("a device is present")
+  from hopper_wgmma import _capi
+  with pytest.raises(RuntimeError):
+    _capi.device_info(0)
+
+
+def test_cfg_struct_layout_matches_header():
+  """The ctypes mirror of bg_cfg has the header's fields in order (sizes: 12 int32, int64, 2 int32)."""
+  import ctypes
+  from hopper_wgmma import _capi
+  text = (ROOT / "include" / "sm100_gemm.h").read_text()
+  body = text[text.index("typedef struct bg_cfg {"):text.index("} bg_cfg;")]
+  fields = re.findall(r"int(?:32|64)_t\s+(\w+);", body)
+  assert [f for f, _ in _capi.BgCfg._fields_] == fields
+  assert ctypes.sizeof(_capi.BgCfg) == 12 * 4 + 8 + 2 * 4
+
+
+# ----------------------------------------------------------------------------------------------------------------
+# configs
+# ----------------------------------------------------------------------------------------------------------------
+def _kw(d):
+  return {k: tuple(v) if isinstance(v, list) else v for k, v in d.items()}
+
+
+def test_wscfg_validation_matches_reference(golden):
+  from hopper_wgmma import WSCfg
+  for case in golden["WSCfg"]:
+    kw = _kw(case["kwargs"])
+    if "error" in case and not case["error"].startswith(SMEM_MSG):
+      with pytest.raises(ValueError) as exc:
+        WSCfg(**kw)
+      assert str(exc.value) == case["error"], kw
+    elif "error" in case:            # the reference's H200 shared-memory budget: ours must reject it too
+      with pytest.raises(ValueError, match=SMEM_MSG):
+        WSCfg(**kw)
+    else:
+      cfg = WSCfg(**kw)
+      assert cfg.BM == case["ok"]["BM"], kw
+      assert cfg.smem_bytes <= 227 * 1024
+
+
+def test_gatedcfg_validation_matches_reference(golden):
+  from hopper_wgmma import GatedCfg
+  for case in golden["GatedCfg"]:
+    kw = case["kwargs"]
+    if "error" in case and not case["error"].startswith(SMEM_MSG):
+      with pytest.raises(ValueError) as exc:
+        GatedCfg(**kw)
+      assert str(exc.value) == case["error"], kw
+    elif "error" not in case:
+      assert GatedCfg(**kw).BM == case["ok"]["BM"], kw
+
+
+def test_b200_knobs_validate():
+  from hopper_wgmma import WSCfg
+  with pytest.raises(ValueError, match="n_mma"):
+    WSCfg(n_mma=3)
+  with pytest.raises(ValueError, match="acc_bufs"):
+    WSCfg(acc_bufs=3)
+  with pytest.raises(ValueError, match="tensor memory"):
+    WSCfg(n_mma=2, acc_bufs=2)
+  assert WSCfg(n_mma=2, cluster=2, tma_store=True).width == 512
+  assert WSCfg().stages_used >= 2 and WSCfg(stages=3).stages_used == 3
+
+
+# ----------------------------------------------------------------------------------------------------------------
+# builders: shape contract and names (no launch)
+# ----------------------------------------------------------------------------------------------------------------
+def test_build_gemm_ws_shape_contract_matches_reference(golden):
+  from hopper_wgmma import WSCfg, build_gemm_ws
+  for case in golden["build_gemm_ws"]:
+    kw = dict(case["kwargs"])
+    N, M, K = case["N"], case["M"], case["K"]
+    if "error" in case and "hilbert needs equal tiles" in case["error"]:
+      # B200 deals Hilbert tiles raggedly over the device's clusters instead of refusing (documented difference)
+      build_gemm_ws(N, WSCfg(**kw), M, K)
+      continue
+    if "error" in case:
+      with pytest.raises(ValueError) as exc:
+        build_gemm_ws(N, WSCfg(**kw), M, K)
+      assert str(exc.value) == case["error"], case
+    else:
+      run = build_gemm_ws(N, WSCfg(**kw), M, K)
+      ref_name = case["ok"]["kernel_name"]
+      assert ("_g1d_" in run.kernel_name) == ("_g1d_" in ref_name)
+      assert run.kernel_name.split("_")[1] == ref_name.split("_")[1]   # the shape token
+      assert run.kernel_name.startswith("sm100_")
+
+
+def test_build_gated_gemm_contract_matches_reference(golden):
+  from hopper_wgmma import GatedCfg, build_gated_gemm
+  for case in golden["build_gated_gemm"]:
+    if "error" in case:
+      with pytest.raises(ValueError) as exc:
+        build_gated_gemm(case["N"], GatedCfg(**case["kwargs"]))
+      assert str(exc.value) == case["error"]
+    else:
+      name = build_gated_gemm(case["N"], GatedCfg(**case["kwargs"])).kernel_name
+      assert name.replace("sm100_", "hopper_") == case["ok"]["kernel_name"]
+
+
+def test_ladder_tables_match_reference(golden):
+  from hopper_wgmma.ladder import EXTRA, LADDER, SWEEP, build
+  assert list(LADDER) == list(golden["LADDER"])
+  assert list(SWEEP) == list(golden["SWEEP"])
+  assert set(golden["EXTRA"]) <= set(EXTRA)
+  b200_defaults = {"num_sm", "stages"}   # device SM count, fill shared memory
+  for table, ref in ((LADDER, golden["LADDER"]), (SWEEP, golden["SWEEP"])):
+    for name, fields in ref.items():
+      cfg = table[name]
+      assert type(cfg).__name__ == fields["type"]
+      for k, v in fields.items():
+        if k == "type" or (k in b200_defaults and type(cfg).__name__ == "WSCfg"): continue
+        got = getattr(cfg, k)
+        assert (list(got) if isinstance(got, tuple) else got) == v, (name, k)
+  with pytest.raises(ValueError) as exc:
+    build(512, LADDER["gated_ws"], 256)
+  assert str(exc.value) == golden["ladder_build"][0]["error"]
+
+
+def test_ring_slot_and_barrier_layout(golden):
+  from hopper_wgmma import Ring
+  ring = Ring(None, 0, golden["Ring_slot"]["stages"], 2, 1)
+  assert [list(ring.slot(j)) for j in range(10)] == golden["Ring_slot"]["slots"]
+  r = Ring(None, 1024, 4)
+  assert [r.full(s) for s in range(4)] == [1024, 1032, 1040, 1048]
+  assert r.empty(0) == 1024 + 32 and r.producer_parity(0) == 1
+
+
+def test_region_semantics():
+  from hopper_wgmma import region
+  assert list(region(True, 0)) == [0] and list(region(False, 0)) == []
+
+
+def test_make_tensor_map_argument_checks_match_reference(golden):
+  from hopper_wgmma.tensor_map import make_tensor_map
+  for case in golden["make_tensor_map"]:
+    with pytest.raises(ValueError) as exc:
+      make_tensor_map(None, *case["args"])
+    assert str(exc.value) == case["error"]
+
+
+def test_runtime_hooks_are_compatible_noops():
+  from hopper_wgmma.runtime import install_runtime_hooks, set_dynamic_smem_bytes
+  install_runtime_hooks()
+  set_dynamic_smem_bytes("sm100_x", 1024)
+  with pytest.raises(ValueError):
+    set_dynamic_smem_bytes("other", 1024)
+  with pytest.raises(ValueError):
+    set_dynamic_smem_bytes("sm100_x", 300 * 1024)
+
+
+# ----------------------------------------------------------------------------------------------------------------
+# tile orders: Python API and the C++ builders the kernel uses, against the reference
+# ----------------------------------------------------------------------------------------------------------------
+def test_python_hilbert_schedule_matches_reference(golden):
+  from hopper_wgmma import hilbert_schedule
+  for case in golden["hilbert_schedule"]:
+    if "error" in case:
+      with pytest.raises(ValueError) as exc:
+        hilbert_schedule(case["M"], case["N"], case["cores"])
+      assert str(exc.value) == case["error"]
+    else:
+      assert hilbert_schedule(case["M"], case["N"], case["cores"]) == case["ok"]
+
+
+def test_cpp_hilbert_order_deals_like_reference(golden):
+  from hopper_wgmma import _capi
+  from oracle import schedule_ref
+  for case in golden["hilbert_schedule"]:
+    curve = _capi.hilbert_order(case["M"], case["N"])
+    assert curve == schedule_ref.hilbert_curve(case["M"], case["N"])
+    if "ok" in case:
+      dealt = schedule_ref.assignment(curve, case["cores"])
+      assert [v for c in dealt for v in c] == case["ok"]
+
+
+def test_cpp_and_python_grouped_orders_match_reference(golden):
+  from hopper_wgmma import _capi
+  from hopper_wgmma.gemm import grouped_tile_order
+  for case in golden["grouped_tile_order"]:
+    CMT, NT, GM, GN = case["CMT"], case["NT"], case["GM"], case["GN"]
+    table = _capi.grouped_order(CMT, NT, GM, GN)
+    assert [[e >> 16, e & 0xFFFF] for e in table] == case["coords"]
+    coords, two_d = grouped_tile_order(CMT, NT, GM, GN)
+    assert two_d == case["grouped_2d"]
+    assert [list(coords(t)) for t in range(CMT * NT)] == case["coords"]
+
+
+def test_cpp_schedule_builders_reject_bad_sizes():
+  from hopper_wgmma import _capi
+  with pytest.raises(ValueError):
+    _capi.grouped_order(4, 4, 5, 1)
+  with pytest.raises(ValueError):
+    _capi.hilbert_order(0, 4)

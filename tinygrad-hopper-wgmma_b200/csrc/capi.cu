@@ -338,11 +338,17 @@ int32_t bg_encode_tensor_map_3d(void* out128, const void* base, int64_t height, 
   return 0;
 }
 
-int32_t bg_plan_create(bg_plan** out, const bg_cfg* cfg, int64_t M, int64_t N, int64_t K, const void* A, int64_t lda,
-                       const void* BT, int64_t ldb, void* C, int64_t ldc, int32_t device) {
-  if (out == nullptr || cfg == nullptr) return fail(-1, "null plan or cfg pointer");
-  *out = nullptr;
-  const bg_cfg& c = *cfg;
+}  // extern "C"
+
+namespace {
+
+// Everything a plan needs except device memory: validation of the knobs and the shape contract, shared-memory and
+// tensor-memory sizing, kernel choice and launch attributes, tensor maps, and the host-side tile table (returned in
+// `sched` with its cache key; empty for the non-persistent kernels). Runs with `device` current. Fills p->kp except
+// its `sched` and `err` pointers, which the caller points at device memory of its own.
+int32_t setup_plan(const bg_cfg& c, int64_t M, int64_t N, int64_t K, const void* A, int64_t lda, const void* BT,
+                   int64_t ldb, void* C, int64_t ldc, int32_t device, bg_plan* p, std::vector<int32_t>& sched,
+                   std::array<int, 6>& sched_key) {
   // ---- knob validation (gemm.py:260-271, gated.py:27-32)
   if (c.kind != BG_KIND_WS && c.kind != BG_KIND_GATED && c.kind != BG_KIND_RING)
     return fail(-1, "unknown kernel kind %d", c.kind);
@@ -412,7 +418,6 @@ int32_t bg_plan_create(bg_plan** out, const bg_cfg* cfg, int64_t M, int64_t N, i
   if (acc_bufs == 0) acc_bufs = 2 * width <= 512 ? 2 : 1;
   if (acc_bufs * width > 512) return fail(-1, "%d accumulators of %d columns exceed tensor memory", acc_bufs, width);
 
-  std::unique_ptr<bg_plan, void (*)(bg_plan*)> p(new bg_plan, free_plan);
   p->device = device;
   p->kind = c.kind;
   p->bm = bm;
@@ -422,14 +427,10 @@ int32_t bg_plan_create(bg_plan** out, const bg_cfg* cfg, int64_t M, int64_t N, i
   p->smem = smem;
   p->threads = c.kind == BG_KIND_RING ? sm100::kRingThreads : sm100::kWsThreads;
 
-  DeviceGuard guard(device);
-  if (guard.status != cudaSuccess) return cuda_fail(guard.status, "cudaSetDevice");
-
   // ---- schedule
   const int64_t tiles = cmt * nt;
   int64_t nclusters = tiles;
-  std::vector<int32_t> sched;
-  std::array<int, 6> sched_key{};
+  sched.clear();
   if (c.kind == BG_KIND_WS) {
     const int num_sm = c.num_sm > 0 ? c.num_sm : sm_count;
     nclusters = std::min<int64_t>(num_sm / cl, tiles);
@@ -503,10 +504,6 @@ int32_t bg_plan_create(bg_plan** out, const bg_cfg* cfg, int64_t M, int64_t N, i
     p->tmC = p->tmA;   // unused by the register epilogue
   }
 
-  // ---- device buffers: tile table and error word
-  if (!sched.empty() && (st = store_table(device, sched_key, sched, &p->d_sched))) return st;
-  if ((st = take_error_word(device, &p->d_err))) return st;
-
   GemmParams& kp = p->kp;
   kp.num_kb = static_cast<int>(nkb);
   kp.bn = bn;
@@ -525,19 +522,43 @@ int32_t bg_plan_create(bg_plan** out, const bg_cfg* cfg, int64_t M, int64_t N, i
   kp.a_stage_bytes = a_stage;
   kp.b_block_bytes = b_block;
   kp.b_stage_bytes = b_stage;
-  kp.sched = p->d_sched;
+  kp.sched = nullptr;
   kp.C = static_cast<__nv_bfloat16*>(C);
   kp.ldc = ldc;
-  kp.err = p->d_err;
+  kp.err = nullptr;
   kp.budget_ns = c.wait_budget_ns > 0 ? static_cast<unsigned long long>(c.wait_budget_ns) : 4000000000ull;
   kp.skip_job = c.debug_skip_job;
 
   snprintf(p->name, sizeof(p->name), "%s<BM=%d,%s,%s> BN=%dx%d stages=%d acc=%d", c.kind == BG_KIND_RING ? "sm100_gemm_ring" : "sm100_gemm_ws",
            bm, paired ? "pair" : (cl == 2 ? "cluster2" : "cta"), p->tma_store ? "tma_store" : "reg_store", bn, nblk,
            stages, acc_bufs);
+  return 0;
+}
+
+}  // namespace
+
+extern "C" {
+
+int32_t bg_plan_create(bg_plan** out, const bg_cfg* cfg, int64_t M, int64_t N, int64_t K, const void* A, int64_t lda,
+                       const void* BT, int64_t ldb, void* C, int64_t ldc, int32_t device) {
+  if (out == nullptr || cfg == nullptr) return fail(-1, "null plan or cfg pointer");
+  *out = nullptr;
+  std::unique_ptr<bg_plan, void (*)(bg_plan*)> p(new bg_plan, free_plan);
+  DeviceGuard guard(device);
+  if (guard.status != cudaSuccess) return cuda_fail(guard.status, "cudaSetDevice");
+  std::vector<int32_t> sched;
+  std::array<int, 6> sched_key{};
+  int32_t st = setup_plan(*cfg, M, N, K, A, lda, BT, ldb, C, ldc, device, p.get(), sched, sched_key);
+  if (st) return st;
+  // ---- device buffers: tile table (cached per schedule) and error word (from the device's slab)
+  if (!sched.empty() && (st = store_table(device, sched_key, sched, &p->d_sched))) return st;
+  if ((st = take_error_word(device, &p->d_err))) return st;
+  p->kp.sched = p->d_sched;
+  p->kp.err = p->d_err;
   *out = p.release();
   return 0;
 }
+
 
 int32_t bg_plan_launch(bg_plan* p, void* stream) {
   if (p == nullptr) return fail(-1, "null plan");

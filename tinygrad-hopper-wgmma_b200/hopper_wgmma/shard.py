@@ -39,7 +39,10 @@ def gather_columns(C_shard, world: int, group=None, as_row_major: bool = True):
   import torch.distributed as dist
   M, n = C_shard.shape
   stack = torch.empty((world, M, n), dtype=C_shard.dtype, device=C_shard.device)
-  dist.all_gather_into_tensor(stack, C_shard.contiguous(), group=group)
+  if dist.get_backend(group) == "nccl":
+    dist.all_gather_into_tensor(stack, C_shard.contiguous(), group=group)
+  else:                                  # gloo (CPU ranks): list form
+    dist.all_gather(list(stack.unbind(0)), C_shard.contiguous(), group=group)
   if not as_row_major: return stack
   return stack.permute(1, 0, 2).reshape(M, world * n)
 
