@@ -131,6 +131,28 @@ int32_t bg_plan_get_info(const bg_plan* plan, bg_plan_info* info);
 void bg_plan_destroy(bg_plan* plan);
 
 /*
+ * bg_gemm_noalloc — the same GEMM as bg_plan_create + bg_plan_launch in one call that allocates no memory.
+ * No counterpart in the reference: it exists for callers that may not allocate device memory themselves, such as a
+ * plugin inside a framework that owns the whole device memory through its own pool allocator (an allocation behind
+ * the pool's back can fail or fragment it), or code on a path where cudaMalloc / cudaFree would synchronize the
+ * device. The caller still passes A, BT and C (as for bg_plan_create); the kernel's scratch — its tile table and
+ * error word — lives in a fixed file-scope device array of this library (256 KiB + 256 bytes per GPU that loads the
+ * library, held until the process exits), so a problem may have at most 65536 tiles (cluster tiles of the schedule);
+ * larger ones are rejected with a negative status before anything is enqueued.
+ *   The first call on a device looks up the array's device address (cudaGetSymbolAddress) with that device current;
+ *   make that first call before any stream capture.
+ *   Every call reuses the same array and overwrites the previous call's tile table and error word (the error word is
+ *   cleared on the stream before each launch). Calls whose kernels can overlap on the GPU — on different streams, or
+ *   from different threads — race on that array: serialize them on one stream.
+ *   The tile table is copied from pageable host memory, so the call waits for work already queued on `stream`.
+ *   err_word == NULL: returns once the GEMM is enqueued. Otherwise it waits for `stream`, stores the kernel's error
+ *   word (0 = ok) and returns a positive status if a device-side wait timed out.
+ */
+int32_t bg_gemm_noalloc(const bg_cfg* cfg, int64_t M, int64_t N, int64_t K, const void* A, int64_t lda,
+                        const void* BT, int64_t ldb, void* C, int64_t ldc, int32_t device, void* stream,
+                        uint32_t* err_word);
+
+/*
  * Host-only schedule builders (no device needed). Entries are (row tile << 16) | column tile.
  * bg_hilbert_order: the tiles of an M x N tile grid in Hilbert-curve order (the walk of gemm.py:222-240); dealing
  *   entry p to cluster p % clusters reproduces hilbert_schedule's assignment, ragged ends included.

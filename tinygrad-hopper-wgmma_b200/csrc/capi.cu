@@ -560,6 +560,80 @@ int32_t bg_plan_create(bg_plan** out, const bg_cfg* cfg, int64_t M, int64_t N, i
 }
 
 
+}  // extern "C"
+
+// ---------------------------------------------------------------------------------------------------------------
+// Allocation-free entry point (bg_gemm_noalloc)
+// ---------------------------------------------------------------------------------------------------------------
+namespace {
+
+// Scratch of bg_gemm_noalloc: the persistent kernel's tile table (kNoAllocMaxTiles int32 entries) followed by its
+// error word. It is a file-scope device array, so every GPU that loads this library holds these 256 KiB + 256 bytes
+// until the process exits, and no call allocates anything.
+constexpr int kNoAllocMaxTiles = 65536;
+constexpr int kNoAllocErrOffset = kNoAllocMaxTiles;   // int32 index of the error word
+static __device__ __align__(256) int32_t g_noalloc_scratch[kNoAllocMaxTiles + 64];
+
+// In host code g_noalloc_scratch names a host-side stand-in, not device memory: its device address is looked up
+// once per device, with that device current, and handed to the kernel.
+struct NoAllocScratch {
+  std::once_flag once;
+  int32_t* ptr = nullptr;
+  cudaError_t status = cudaSuccess;
+};
+
+NoAllocScratch& noalloc_scratch(int dev) {
+  static NoAllocScratch s[64];
+  return s[dev & 63];
+}
+
+}  // namespace
+
+extern "C" {
+
+int32_t bg_gemm_noalloc(const bg_cfg* cfg, int64_t M, int64_t N, int64_t K, const void* A, int64_t lda,
+                        const void* BT, int64_t ldb, void* C, int64_t ldc, int32_t device, void* stream,
+                        uint32_t* err_word) {
+  if (cfg == nullptr) return fail(-1, "null cfg pointer");
+  if (device < 0 || device >= 64) return fail(-1, "device %d out of range", device);
+  DeviceGuard guard(device);
+  if (guard.status != cudaSuccess) return cuda_fail(guard.status, "cudaSetDevice");
+  bg_plan plan;   // lives on this stack frame and owns no device memory
+  std::vector<int32_t> sched;
+  std::array<int, 6> sched_key{};
+  int32_t st = setup_plan(*cfg, M, N, K, A, lda, BT, ldb, C, ldc, device, &plan, sched, sched_key);
+  if (st) return st;
+  if (sched.size() > static_cast<size_t>(kNoAllocMaxTiles))
+    return fail(-1, "bg_gemm_noalloc: %zu tiles exceed its fixed scratch of %d tile entries; use bg_plan_create or "
+                "wider tiles", sched.size(), kNoAllocMaxTiles);
+  NoAllocScratch& ns = noalloc_scratch(device);
+  std::call_once(ns.once, [&ns] {
+    ns.status = cudaGetSymbolAddress(reinterpret_cast<void**>(&ns.ptr), g_noalloc_scratch);
+  });
+  if (ns.status != cudaSuccess) return cuda_fail(ns.status, "cudaGetSymbolAddress(g_noalloc_scratch)");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  unsigned int* err = reinterpret_cast<unsigned int*>(ns.ptr + kNoAllocErrOffset);
+  cudaError_t e;
+  if (!sched.empty()) {
+    // From pageable host memory: the copy waits for work already queued on the stream, and the table may be freed
+    // as soon as cudaMemcpyAsync returns.
+    e = cudaMemcpyAsync(ns.ptr, sched.data(), sched.size() * sizeof(int32_t), cudaMemcpyHostToDevice, s);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyAsync(tile table)");
+  }
+  if ((e = cudaMemsetAsync(err, 0, sizeof(unsigned int), s)) != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync");
+  plan.kp.sched = sched.empty() ? nullptr : ns.ptr;
+  plan.kp.err = err;
+  if ((st = bg_plan_launch(&plan, stream))) return st;
+  if (err_word == nullptr) return 0;
+  if ((e = cudaStreamSynchronize(s)) != cudaSuccess) return cuda_fail(e, "cudaStreamSynchronize");
+  uint32_t w = 0;
+  if ((e = cudaMemcpy(&w, err, sizeof(w), cudaMemcpyDeviceToHost)) != cudaSuccess)
+    return cuda_fail(e, "cudaMemcpy(error word)");
+  *err_word = w;
+  if (w != 0) return fail(6, "device wait timed out (error word 0x%08x)", w);
+  return 0;
+}
+
 int32_t bg_plan_launch(bg_plan* p, void* stream) {
   if (p == nullptr) return fail(-1, "null plan");
   DeviceGuard guard(p->device);
