@@ -54,6 +54,8 @@ enum {
  *   n_mma       tcgen05.mma instructions along N per K step (1 or 2; persistent kernel only): a tile is n_mma * BN
  *               columns wide, so n_mma = 2 with BN = 256 gives 128 x 512 per CTA (256 x 512 per CTA pair), which
  *               reads 25% fewer operand bytes per FLOP than 256 x 256 at the cost of a single TMEM accumulator
+ *   no_tail_split   0 (default): when the persistent schedule's last wave is at most half full, its tiles are split
+ *                   into half-width tiles so that the tail costs about half a tile; 1: keep whole tiles
  *   debug_skip_job  test hook: the producer never loads this job (-1 = off) so that the kernel's waits run out and
  *                   the launch reports an error instead of hanging
  */
@@ -73,6 +75,8 @@ typedef struct bg_cfg {
   int64_t wait_budget_ns;
   int32_t debug_skip_job;
   int32_t n_mma;
+  int32_t no_tail_split;
+  int32_t reserved;
 } bg_cfg;
 
 /* What a plan resolved to (for reports and tests). */
@@ -90,6 +94,7 @@ typedef struct bg_plan_info {
   int32_t acc_bufs;       /* accumulator buffers                             */
   int32_t tmem_cols;      /* tensor-memory columns allocated per CTA         */
   int32_t max_active_clusters; /* occupancy limit reported by the runtime (0 if not queried) */
+  int32_t narrow_tiles;   /* half-width tiles in the last wave (0 = no tail split)             */
   char kernel[96];        /* kernel family and template arguments            */
 } bg_plan_info;
 

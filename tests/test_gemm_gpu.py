@@ -113,13 +113,18 @@ def _b200_cases():
     ("wide_pair_hilbert_ragged", WSCfg(BN=128, n_mma=2, cluster=2, tma_store=True, hilbert=True, num_sm=6),
      (768, 1280, 192)),
     ("wide_c1_bn80", WSCfg(BN=80, n_mma=2, consumers=1), (128, 320, 64)),
+    ("no_tail_split", WSCfg(tma_store=True, cluster=2, split_tail=False), (512, 512, 512)),
+    ("tail_split_cta", WSCfg(BN=128, tma_store=True, num_sm=6), (512, 640, 192)),
+    ("tail_split_pair", WSCfg(tma_store=True, cluster=2, hilbert=True, num_sm=18), (1024, 1792, 128)),
+    ("tail_split_wide_pair", WSCfg(n_mma=2, cluster=2, tma_store=True, num_sm=10), (1024, 1536, 128)),
+    ("tail_split_bm64_reg", WSCfg(consumers=1, BN=128, num_sm=7), (320, 384, 128)),
     ("gated_c1", GatedCfg(consumers=1, BN=128), (512, 512, 512)),
     ("ring_bn256", GatedCfg(consumers=0, BN=256, stages=2), (256, 256, 256)),
     ("ring_bn64", GatedCfg(consumers=0, BN=64, stages=3), (192, 192, 192)),
   ]
 
 
-@pytest.mark.parametrize("idx", range(23))
+@pytest.mark.parametrize("idx", range(28))
 def test_b200_cases(idx, cuda_dev):
   from hopper_wgmma.ladder import build
   name, cfg, (M, N, K) = _b200_cases()[idx]

@@ -47,7 +47,7 @@ def test_cfg_struct_layout_matches_header():
   body = text[text.index("typedef struct bg_cfg {"):text.index("} bg_cfg;")]
   fields = re.findall(r"int(?:32|64)_t\s+(\w+);", body)
   assert [f for f, _ in _capi.BgCfg._fields_] == fields
-  assert ctypes.sizeof(_capi.BgCfg) == 12 * 4 + 8 + 2 * 4
+  assert ctypes.sizeof(_capi.BgCfg) == 12 * 4 + 8 + 4 * 4
 
 
 # ----------------------------------------------------------------------------------------------------------------

@@ -133,7 +133,8 @@ void grouped_order(int mt, int nt, int gm, int gn, std::vector<int32_t>& out) {
 // ---------------------------------------------------------------------------------------------------------------
 // Kernel table
 // ---------------------------------------------------------------------------------------------------------------
-using WsKernel = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const GemmParams);
+using WsKernel = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const CUtensorMap,
+                          const GemmParams);
 using RingKernel = void (*)(const CUtensorMap, const CUtensorMap, const GemmParams);
 
 template <int NB>
@@ -178,7 +179,8 @@ struct bg_plan {
   int threads = 0;
   size_t smem = 0;
   int max_active_clusters = 0;
-  CUtensorMap tmA{}, tmB{}, tmC{};
+  CUtensorMap tmA{}, tmB{}, tmBn{}, tmC{};
+  int narrow_tiles = 0;
   GemmParams kp{};
   int32_t* d_sched = nullptr;
   unsigned int* d_err = nullptr;
@@ -212,7 +214,7 @@ struct DeviceGuard {
 //   * error words, one per live plan, handed out from 4 KiB slabs and returned when the plan is destroyed.
 struct DeviceStore {
   std::mutex mu;
-  std::map<std::array<int, 6>, int32_t*> tables;
+  std::map<std::array<int, 8>, int32_t*> tables;
   std::vector<unsigned int*> free_words;
 };
 
@@ -221,7 +223,7 @@ DeviceStore& device_store(int dev) {
   return stores[dev & 63];
 }
 
-int32_t store_table(int dev, const std::array<int, 6>& key, const std::vector<int32_t>& host, int32_t** out) {
+int32_t store_table(int dev, const std::array<int, 8>& key, const std::vector<int32_t>& host, int32_t** out) {
   DeviceStore& s = device_store(dev);
   std::lock_guard<std::mutex> lock(s.mu);
   auto it = s.tables.find(key);
@@ -348,7 +350,7 @@ namespace {
 // its `sched` and `err` pointers, which the caller points at device memory of its own.
 int32_t setup_plan(const bg_cfg& c, int64_t M, int64_t N, int64_t K, const void* A, int64_t lda, const void* BT,
                    int64_t ldb, void* C, int64_t ldc, int32_t device, bg_plan* p, std::vector<int32_t>& sched,
-                   std::array<int, 6>& sched_key) {
+                   std::array<int, 8>& sched_key) {
   // ---- knob validation (gemm.py:260-271, gated.py:27-32)
   if (c.kind != BG_KIND_WS && c.kind != BG_KIND_GATED && c.kind != BG_KIND_RING)
     return fail(-1, "unknown kernel kind %d", c.kind);
@@ -433,14 +435,14 @@ int32_t setup_plan(const bg_cfg& c, int64_t M, int64_t N, int64_t K, const void*
   sched.clear();
   if (c.kind == BG_KIND_WS) {
     const int num_sm = c.num_sm > 0 ? c.num_sm : sm_count;
-    nclusters = std::min<int64_t>(num_sm / cl, tiles);
+    nclusters = num_sm / cl;   // clusters available; the grid is cut to the schedule's entries below
     if (c.hilbert) {
-      sched_key = {device, 1, static_cast<int>(cmt), static_cast<int>(nt), 0, 0};
+      sched_key = {device, 1, static_cast<int>(cmt), static_cast<int>(nt), 0, 0, 0, 0};
       hilbert_order(static_cast<int>(cmt), static_cast<int>(nt), sched);
     } else {
       const int gm = std::min<int>(std::max(c.group_m / cl, 1), static_cast<int>(cmt));
       const int gn = std::min<int>(c.group_n, static_cast<int>(nt));
-      sched_key = {device, 0, static_cast<int>(cmt), static_cast<int>(nt), gm, gn};
+      sched_key = {device, 0, static_cast<int>(cmt), static_cast<int>(nt), gm, gn, 0, 0};
       grouped_order(static_cast<int>(cmt), static_cast<int>(nt), gm, gn, sched);
     }
   }
@@ -493,11 +495,41 @@ int32_t setup_plan(const bg_cfg& c, int64_t M, int64_t N, int64_t K, const void*
     p->max_active_clusters = maxc;
     if (c.kind == BG_KIND_WS) nclusters = std::min<int64_t>(nclusters, maxc);
   }
+  // ---- wave-quantization tail: the last, partial wave of the persistent schedule (entries [full, tiles) of the
+  // dealt table) is split into half-width tiles when twice its size still fits in one wave, so that the tail takes
+  // about half a tile's time instead of a whole one. Half width = one N block when nblk == 2, MMA N = BN/2 otherwise.
+  const int half = nblk == 2 ? bn : bn / 2;
+  const bool narrow_ok = nblk == 2 || (half % 16 == 0 && (!c.tma_store || half % 64 == 0));
+  int64_t n_entries = tiles;
+  if (c.kind == BG_KIND_WS && !c.no_tail_split && narrow_ok && !sched.empty()) {
+    const int64_t full = (tiles / nclusters) * nclusters;
+    const int64_t tail = tiles - full;
+    if (tail > 0 && 2 * tail <= nclusters) {
+      std::vector<int32_t> split(sched.begin(), sched.begin() + full);
+      for (int64_t i = full; i < tiles; ++i) {
+        const int32_t cmi = sched[i] >> 16, tni = sched[i] & 0xFFFF;
+        split.push_back((cmi << 16) | sm100::kNarrowTile | (2 * tni));
+        split.push_back((cmi << 16) | sm100::kNarrowTile | (2 * tni + 1));
+      }
+      sched.swap(split);
+      n_entries = static_cast<int64_t>(sched.size());
+      p->narrow_tiles = static_cast<int>(2 * tail);
+      sched_key[6] = static_cast<int>(nclusters);
+      sched_key[7] = 1;
+    }
+  }
+  if (nt * 2 > 0x7FFF) return fail(-1, "too many column tiles (%lld) for the tile table", (long long)nt);
+  nclusters = std::min<int64_t>(nclusters, n_entries);
   p->grid = static_cast<int>(nclusters * (c.kind == BG_KIND_RING ? 1 : cl));
 
   // ---- tensor maps: A[M,K] box (64, BM); BT[N,K] box (64, bn_local); C[M,N] box (64, BM/4) per epilogue warp
   if ((st = encode_2d(&p->tmA, A, K, M, lda, 64, bm, "A"))) return st;
   if ((st = encode_2d(&p->tmB, BT, K, N, ldb, 64, bn_local, "BT"))) return st;
+  if (nblk == 1 && p->narrow_tiles > 0) {
+    if ((st = encode_2d(&p->tmBn, BT, K, N, ldb, 64, bn_local / 2, "BT half tiles"))) return st;
+  } else {
+    p->tmBn = p->tmB;
+  }
   if (p->tma_store) {
     if ((st = encode_2d(&p->tmC, C, N, M, ldc, 64, bm / 4, "C"))) return st;
   } else {
@@ -510,7 +542,7 @@ int32_t setup_plan(const bg_cfg& c, int64_t M, int64_t N, int64_t K, const void*
   kp.nblk = nblk;
   kp.bn_local = bn_local;
   kp.stages = stages;
-  kp.tiles = static_cast<int>(tiles);
+  kp.tiles = static_cast<int>(n_entries);
   kp.nclusters = static_cast<int>(nclusters);
   kp.cl = c.kind == BG_KIND_RING ? 1 : cl;
   kp.nt = static_cast<int>(nt);
@@ -519,6 +551,8 @@ int32_t setup_plan(const bg_cfg& c, int64_t M, int64_t N, int64_t K, const void*
   kp.tmem_cols = pow2_cols(acc_bufs * width);
   kp.idesc = make_idesc(paired ? 2 * bm : bm, bn);
   kp.tx_bytes = (a_stage + b_stage) * (paired ? 2u : 1u);
+  kp.tx_narrow = (a_stage + (nblk == 2 ? b_block : b_block / 2)) * (paired ? 2u : 1u);
+  kp.idesc_narrow = make_idesc(paired ? 2 * bm : bm, nblk == 2 ? bn : bn / 2);
   kp.a_stage_bytes = a_stage;
   kp.b_block_bytes = b_block;
   kp.b_stage_bytes = b_stage;
@@ -529,9 +563,9 @@ int32_t setup_plan(const bg_cfg& c, int64_t M, int64_t N, int64_t K, const void*
   kp.budget_ns = c.wait_budget_ns > 0 ? static_cast<unsigned long long>(c.wait_budget_ns) : 4000000000ull;
   kp.skip_job = c.debug_skip_job;
 
-  snprintf(p->name, sizeof(p->name), "%s<BM=%d,%s,%s> BN=%dx%d stages=%d acc=%d", c.kind == BG_KIND_RING ? "sm100_gemm_ring" : "sm100_gemm_ws",
+  snprintf(p->name, sizeof(p->name), "%s<BM=%d,%s,%s> BN=%dx%d stages=%d acc=%d tail=%d", c.kind == BG_KIND_RING ? "sm100_gemm_ring" : "sm100_gemm_ws",
            bm, paired ? "pair" : (cl == 2 ? "cluster2" : "cta"), p->tma_store ? "tma_store" : "reg_store", bn, nblk,
-           stages, acc_bufs);
+           stages, acc_bufs, p->narrow_tiles);
   return 0;
 }
 
@@ -547,7 +581,7 @@ int32_t bg_plan_create(bg_plan** out, const bg_cfg* cfg, int64_t M, int64_t N, i
   DeviceGuard guard(device);
   if (guard.status != cudaSuccess) return cuda_fail(guard.status, "cudaSetDevice");
   std::vector<int32_t> sched;
-  std::array<int, 6> sched_key{};
+  std::array<int, 8> sched_key{};
   int32_t st = setup_plan(*cfg, M, N, K, A, lda, BT, ldb, C, ldc, device, p.get(), sched, sched_key);
   if (st) return st;
   // ---- device buffers: tile table (cached per schedule) and error word (from the device's slab)
@@ -600,7 +634,7 @@ int32_t bg_gemm_noalloc(const bg_cfg* cfg, int64_t M, int64_t N, int64_t K, cons
   if (guard.status != cudaSuccess) return cuda_fail(guard.status, "cudaSetDevice");
   bg_plan plan;   // lives on this stack frame and owns no device memory
   std::vector<int32_t> sched;
-  std::array<int, 6> sched_key{};
+  std::array<int, 8> sched_key{};
   int32_t st = setup_plan(*cfg, M, N, K, A, lda, BT, ldb, C, ldc, device, &plan, sched, sched_key);
   if (st) return st;
   if (sched.size() > static_cast<size_t>(kNoAllocMaxTiles))
@@ -657,7 +691,7 @@ int32_t bg_plan_launch(bg_plan* p, void* stream) {
   if (p->kind == BG_KIND_RING)
     e = cudaLaunchKernelEx(&lc, p->ring, p->tmA, p->tmB, p->kp);
   else
-    e = cudaLaunchKernelEx(&lc, p->ws, p->tmA, p->tmB, p->tmC, p->kp);
+    e = cudaLaunchKernelEx(&lc, p->ws, p->tmA, p->tmB, p->tmBn, p->tmC, p->kp);
   if (e != cudaSuccess) return cuda_fail(e, "cudaLaunchKernelEx");
   return 0;
 }
@@ -698,6 +732,7 @@ int32_t bg_plan_get_info(const bg_plan* p, bg_plan_info* info) {
   info->acc_bufs = p->kp.acc_bufs;
   info->tmem_cols = static_cast<int32_t>(p->kp.tmem_cols);
   info->max_active_clusters = p->max_active_clusters;
+  info->narrow_tiles = p->narrow_tiles;
   snprintf(info->kernel, sizeof(info->kernel), "%s", p->name);
   return 0;
 }

@@ -58,11 +58,14 @@ struct GemmParams {
   uint32_t tmem_cols;      // TMEM columns allocated (power of two >= 32)
   uint32_t idesc;          // tcgen05 instruction descriptor (bf16 x bf16 -> f32, K-major, M, N)
   uint32_t tx_bytes;       // bytes that complete one stage's FULL barrier (both CTAs' loads when PAIRED)
+  uint32_t tx_narrow;      // the same for a half-width tile
+  uint32_t idesc_narrow;   // instruction descriptor of a half-width tile (N = bn / 2) when nblk == 1
   uint32_t a_stage_bytes;  // BM * 128
   uint32_t b_block_bytes;  // bn_local * 128: one N block of B in a stage
   uint32_t b_stage_bytes;  // nblk * b_block_bytes
   const int32_t* sched;    // [tiles] entries (cluster row tile << 16) | column tile; entry i runs on cluster
-                           // i % nclusters as that cluster's (i / nclusters)-th tile
+                           // i % nclusters as that cluster's (i / nclusters)-th tile. kNarrowTile in the column
+                           // field marks a half-width tile whose column index counts half-width tiles
   __nv_bfloat16* C;        // output base (register epilogue)
   long long ldc;           // C row pitch in elements
   unsigned int* err;       // error word (0 = ok)
@@ -74,15 +77,24 @@ __device__ __forceinline__ void record_error(unsigned int* err, uint32_t role, u
   atomicCAS(err, 0u, role | (counter > 0xFFFFFFu ? 0xFFFFFFu : counter));
 }
 
-__device__ __forceinline__ void tile_coords(const GemmParams& p, int idx, int& cm, int& tn) {
+constexpr int kNarrowTile = 0x8000;   // column-field flag of a half-width tile (the last wave's split tiles)
+
+__device__ __forceinline__ void tile_coords(const GemmParams& p, int idx, int& cm, int& tn, bool& narrow) {
   if (p.sched != nullptr) {
     const int e = __ldg(p.sched + idx);
     cm = e >> 16;
-    tn = e & 0xFFFF;
+    tn = e & 0x7FFF;
+    narrow = (e & kNarrowTile) != 0;
   } else {
     cm = idx / p.nt;
     tn = idx - cm * p.nt;
+    narrow = false;
   }
+}
+
+__device__ __forceinline__ void tile_coords(const GemmParams& p, int idx, int& cm, int& tn) {
+  bool narrow;
+  tile_coords(p, idx, cm, tn, narrow);
 }
 
 // Round 2N fp32 accumulator words to bf16 and store N/2 packed words per 16-byte chunk.
@@ -115,7 +127,8 @@ __device__ __forceinline__ void epilogue_registers(uint32_t tacc, __nv_bfloat16*
 template <int BM, bool PAIRED, bool TMA_STORE, int NB>
 __global__ void __launch_bounds__(kWsThreads, 1)
     sm100_gemm_ws(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                  const __grid_constant__ CUtensorMap tmC, const GemmParams p) {
+                  const __grid_constant__ CUtensorMap tmBn, const __grid_constant__ CUtensorMap tmC,
+                  const GemmParams p) {
   static_assert(BM == 64 || BM == 128, "BM is 64 or 128 rows per CTA");
   static_assert(!PAIRED || BM == 128, "CTA pairs use M = 256 (128 rows per CTA)");
   constexpr int CG = PAIRED ? 2 : 1;
@@ -159,6 +172,7 @@ __global__ void __launch_bounds__(kWsThreads, 1)
   if (warp == 0 && lane == 0) {
     tma_prefetch_map(&tmA);
     tma_prefetch_map(&tmB);
+    if (NB == 1) tma_prefetch_map(&tmBn);
     if (TMA_STORE) tma_prefetch_map(&tmC);
   }
   if (warp == 1) {
@@ -180,9 +194,16 @@ __global__ void __launch_bounds__(kWsThreads, 1)
       const int idx = cid + i * p.nclusters;
       if (idx >= p.tiles) break;
       int cm, tn;
-      tile_coords(p, idx, cm, tn);
+      bool narrow;
+      tile_coords(p, idx, cm, tn, narrow);
+      // A half-width tile keeps NB == 2's MMA N and drops the second N block, or halves NB == 1's MMA N
+      const int nblk = (narrow && NB == 2) ? 1 : NB;
+      const CUtensorMap* mapB = (narrow && NB == 1) ? &tmBn : &tmB;
+      const int bsub = (narrow && NB == 1) ? p.bn / 2 : p.bn;            // B rows of one N block (pair level)
+      const int width = narrow ? p.bn * NB / 2 : p.bn * NB;
+      const uint32_t tx = narrow ? p.tx_narrow : p.tx_bytes;
       const int row_a = (cm * p.cl + static_cast<int>(rank)) * BM;
-      const int row_b = tn * p.bn * NB + (PAIRED ? static_cast<int>(rank) * p.bn_local : 0);
+      const int row_b = tn * width + (PAIRED ? static_cast<int>(rank) * (bsub / 2) : 0);
       for (int kb = 0; kb < p.num_kb; ++kb, ++job) {
         if (!mbar_wait_warp(empty0 + 8u * stage, phase ^ 1u, budget)) {
           if (lane == 0) record_error(p.err, kErrProducer, job);
@@ -195,17 +216,17 @@ __global__ void __launch_bounds__(kWsThreads, 1)
           const uint32_t b_dst = sB + stage * p.b_stage_bytes;
           if (PAIRED) {
             const uint32_t fb_leader = mapa_shared(fb, 0);
-            if (leader) mbar_arrive_expect_tx(fb, p.tx_bytes);
+            if (leader) mbar_arrive_expect_tx(fb, tx);
             tma_load_2d_pair(a_dst, &tmA, fb_leader, kb * kBK, row_a);
 #pragma unroll
             for (int nb = 0; nb < NB; ++nb)
-              tma_load_2d_pair(b_dst + nb * p.b_block_bytes, &tmB, fb_leader, kb * kBK, row_b + nb * p.bn);
+              if (nb < nblk) tma_load_2d_pair(b_dst + nb * p.b_block_bytes, mapB, fb_leader, kb * kBK, row_b + nb * bsub);
           } else {
-            mbar_arrive_expect_tx(fb, p.tx_bytes);
+            mbar_arrive_expect_tx(fb, tx);
             tma_load_2d(a_dst, &tmA, fb, kb * kBK, row_a);
 #pragma unroll
             for (int nb = 0; nb < NB; ++nb)
-              tma_load_2d(b_dst + nb * p.b_block_bytes, &tmB, fb, kb * kBK, row_b + nb * p.bn);
+              if (nb < nblk) tma_load_2d(b_dst + nb * p.b_block_bytes, mapB, fb, kb * kBK, row_b + nb * bsub);
           }
         }
         __syncwarp();
@@ -237,6 +258,11 @@ __global__ void __launch_bounds__(kWsThreads, 1)
       for (int i = 0; !failed; ++i) {
         const int idx = cid + i * p.nclusters;
         if (idx >= p.tiles) break;
+        int cm, tn;
+        bool narrow;
+        tile_coords(p, idx, cm, tn, narrow);
+        const int nblk = (narrow && NB == 2) ? 1 : NB;
+        const uint32_t idesc = (narrow && NB == 1) ? p.idesc_narrow : p.idesc;
         if (!mbar_wait_warp(tempty0 + 8u * acc, acc_phase ^ 1u, budget)) {
           if (lane == 0) record_error(p.err, kErrMmaAcc, i);
           break;
@@ -259,9 +285,10 @@ __global__ void __launch_bounds__(kWsThreads, 1)
             for (int k = 0; k < kBK / 16; ++k)
 #pragma unroll
               for (int nb = 0; nb < NB; ++nb)
-                mma_bf16<CG>(d + static_cast<uint32_t>(nb * p.bn), ad + 2u * k,
-                             bd + static_cast<uint64_t>((nb * p.b_block_bytes) >> 4) + 2u * k, p.idesc,
-                             (kb | k) != 0 ? 1u : 0u);
+                if (nb < nblk)
+                  mma_bf16<CG>(d + static_cast<uint32_t>(nb * p.bn), ad + 2u * k,
+                               bd + static_cast<uint64_t>((nb * p.b_block_bytes) >> 4) + 2u * k, idesc,
+                               (kb | k) != 0 ? 1u : 0u);
             mma_commit<CG>(empty0 + 8u * stage);
             if (PAIRED) mma_commit<CG>(mapa_shared(empty0 + 8u * stage, 1));
           }
@@ -297,9 +324,10 @@ __global__ void __launch_bounds__(kWsThreads, 1)
       const int idx = cid + i * p.nclusters;
       if (idx >= p.tiles) break;
       int cm, tn;
-      tile_coords(p, idx, cm, tn);
+      bool narrow;
+      tile_coords(p, idx, cm, tn, narrow);
       const int row0 = (cm * p.cl + static_cast<int>(rank)) * BM + q * ROWS_W;   // first row of this warp
-      const int width = p.bn * NB;   // output columns of this tile
+      const int width = narrow ? p.bn * NB / 2 : p.bn * NB;   // output columns of this tile
       const int col0 = tn * width;
       if (!mbar_wait_warp(tfull0 + 8u * acc, acc_phase, budget)) {
         record_error(p.err, kErrEpilogue, i);

@@ -24,7 +24,8 @@ class BgCfg(ctypes.Structure):
               ("consumers", ctypes.c_int32), ("num_sm", ctypes.c_int32), ("group_m", ctypes.c_int32),
               ("group_n", ctypes.c_int32), ("tma_store", ctypes.c_int32), ("cluster", ctypes.c_int32),
               ("hilbert", ctypes.c_int32), ("acc_bufs", ctypes.c_int32), ("wait_budget_ns", ctypes.c_int64),
-              ("debug_skip_job", ctypes.c_int32), ("n_mma", ctypes.c_int32)]
+              ("debug_skip_job", ctypes.c_int32), ("n_mma", ctypes.c_int32),
+              ("no_tail_split", ctypes.c_int32), ("reserved", ctypes.c_int32)]
 
 
 class BgPlanInfo(ctypes.Structure):
@@ -32,7 +33,7 @@ class BgPlanInfo(ctypes.Structure):
               ("stages", ctypes.c_int32), ("tiles", ctypes.c_int32), ("clusters", ctypes.c_int32),
               ("cluster", ctypes.c_int32), ("paired", ctypes.c_int32), ("bm", ctypes.c_int32), ("bn", ctypes.c_int32),
               ("acc_bufs", ctypes.c_int32), ("tmem_cols", ctypes.c_int32), ("max_active_clusters", ctypes.c_int32),
-              ("kernel", ctypes.c_char * 96)]
+              ("narrow_tiles", ctypes.c_int32), ("kernel", ctypes.c_char * 96)]
 
 
 def _load() -> ctypes.CDLL:

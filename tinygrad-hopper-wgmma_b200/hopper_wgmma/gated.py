@@ -51,7 +51,8 @@ class GatedCfg:
     kind = _capi.KIND_GATED if self.consumers else _capi.KIND_RING
     return _capi.BgCfg(kind=kind, BN=self.BN, BK=self.BK, stages=self.stages, consumers=self.consumers, num_sm=0,
                        group_m=1, group_n=1, tma_store=0, cluster=1, hilbert=0, acc_bufs=1,
-                       wait_budget_ns=wait_budget_ns, debug_skip_job=debug_skip_job, n_mma=1)
+                       wait_budget_ns=wait_budget_ns, debug_skip_job=debug_skip_job, n_mma=1,
+                       no_tail_split=1)
 
 
 def build_gated_gemm(N: int, cfg: GatedCfg, *, wait_budget_ns: int = 0, debug_skip_job: int = -1):

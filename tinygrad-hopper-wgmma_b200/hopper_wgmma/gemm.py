@@ -142,6 +142,7 @@ class WSCfg:
   hilbert: bool = False        # Hilbert tile order from a host-built table
   acc_bufs: int | None = None  # accumulator buffers in tensor memory; None = 2 when 2 * width <= 512 columns
   n_mma: int = 1               # tcgen05.mma instructions along N per K step: tiles are n_mma * BN columns wide
+  split_tail: bool = True      # split a last wave that is at most half full into half-width tiles
 
   def __post_init__(self):
     if self.BK != 64: raise ValueError("BK must be 64 (one 128-byte swizzle atom)")
@@ -201,7 +202,7 @@ class WSCfg:
                        num_sm=num_sm or self.num_sm or 0, group_m=self.group_m, group_n=self.group_n,
                        tma_store=int(self.tma_store), cluster=self.cluster, hilbert=int(self.hilbert),
                        acc_bufs=self.acc_bufs or 0, wait_budget_ns=wait_budget_ns, debug_skip_job=debug_skip_job,
-                       n_mma=self.n_mma)
+                       n_mma=self.n_mma, no_tail_split=0 if self.split_tail else 1)
 
 
 # =============================================================================================================

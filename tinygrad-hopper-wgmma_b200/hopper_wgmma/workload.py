@@ -18,6 +18,7 @@ from __future__ import annotations
 
 import argparse
 import json
+import statistics
 
 
 def parse_shape(text: str) -> tuple[int, int, int]:
@@ -25,6 +26,28 @@ def parse_shape(text: str) -> tuple[int, int, int]:
   if len(dims) == 1: dims *= 3
   if len(dims) != 3: raise SystemExit(f"bad --shape {text!r}")
   return dims[0], dims[1], dims[2]
+
+
+def _time_pair(fn, ref_fn, reps: int, warmup: int, flush=None) -> tuple[list[float], list[float]]:
+  """Alternate ``fn`` and ``ref_fn`` launch by launch (each timed alone with CUDA events), so that both see the same
+  clock and power state; returns both lists of microseconds."""
+  import torch
+  for _ in range(warmup):
+    fn()
+    ref_fn()
+  ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(reps)]
+  torch.cuda.synchronize()
+  for e in ev:
+    if flush is not None: flush.zero_()
+    e[0].record()
+    fn()
+    e[1].record()
+    if flush is not None: flush.zero_()
+    e[2].record()
+    ref_fn()
+    e[3].record()
+  torch.cuda.synchronize()
+  return [e[0].elapsed_time(e[1]) * 1e3 for e in ev], [e[2].elapsed_time(e[3]) * 1e3 for e in ev]
 
 
 def _time(fn, reps: int, warmup: int, flush=None) -> tuple[float, float]:
@@ -98,10 +121,16 @@ def main(argv=None) -> int:
       launch.check()
       print(f"KERNEL {name} {run.kernel_name} {launch.info()['kernel']}", flush=True)
       if args.time:
-        best, mean = _time(launch, args.reps, args.warmup, flush)
-        rec = {"label": name, "shape": [M, N, K], "kernel": launch.info()["kernel"], "us_best": round(best, 2),
-               "us_mean": round(mean, 2), "tflops": round(flops / best / 1e6, 1)}
-        if cub_us: rec["pct_cublas"] = round(100.0 * cub_us / best, 1)
+        rec = {"label": name, "shape": [M, N, K], "kernel": launch.info()["kernel"]}
+        if args.torch:   # interleaved with cuBLAS: the ratio of medians is robust to clock drift
+          ours, cub = _time_pair(launch, lambda: torch.matmul(a, b, out=out), args.reps, args.warmup, flush)
+          med, cmed = statistics.median(ours), statistics.median(cub)
+          rec.update(us_best=round(min(ours), 2), us_median=round(med, 2), tflops=round(flops / med / 1e6, 1),
+                     cublas_us_median=round(cmed, 2), cublas_tflops=round(flops / cmed / 1e6, 1),
+                     pct_cublas=round(100.0 * cmed / med, 1))
+        else:
+          best, mean = _time(launch, args.reps, args.warmup, flush)
+          rec.update(us_best=round(best, 2), us_mean=round(mean, 2), tflops=round(flops / best / 1e6, 1))
         print("TIME " + json.dumps(rec), flush=True)
     except ValueError as exc:
       print(f"SKIP {name}: {exc}", flush=True)
