@@ -65,14 +65,15 @@ def measured_peaks() -> dict:
   return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
 
 
-def profiled_traffic(kernel_tag: str, flops_per_launch: float):
-  """DRAM bytes per launch from the committed ncu summary (profiles/*.txt lines 'traffic <tag> <bytes> <flops>'),
-  scaled by the FLOPs processed when the capture ran a different size."""
+def profiled_traffic(kernel_tag: str, workload: str, flops_per_launch: float):
+  """DRAM bytes (read + write) per launch of this kernel on this workload, from the committed ncu summaries
+  (profiles/*.txt lines 'traffic <kernel tag> <workload> <bytes> <flops of the captured launch>'), scaled to this
+  launch's FLOPs when the capture ran a per-rank shard of a different width. None if no capture covers it."""
   for f in sorted((ROOT / "profiles").glob("*.txt")):
     for line in f.read_text().splitlines():
       parts = line.split()
-      if len(parts) == 4 and parts[0] == "traffic" and parts[1] == kernel_tag:
-        return float(parts[2]) * flops_per_launch / float(parts[3])
+      if len(parts) == 5 and parts[0] == "traffic" and parts[1] == kernel_tag and parts[2] == workload:
+        return round(float(parts[3]) * flops_per_launch / float(parts[4]))
   return None
 
 
@@ -173,7 +174,7 @@ def run_reference(args):
   tflops = 2.0 * cap_M * n * K * args.steps / dt / 1e12
   cores = blas_threads()
   sample = f"{args.steps} x numpy fp32 GEMM {cap_M}x{n}x{K} + bf16 rounding (rows capped at {cap_M} of {M})"
-  print(json.dumps({
+  emit({
     "impl": "reference", "metric": METRIC, "value": round(tflops, 4), "unit": "TFLOPS", "n_gpus": args.gpus,
     "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 3),
     "higher_is_better": True, "scaling": scaling, "vs_baseline": None, "dtype": "bf16 in, fp32 accumulate",
@@ -182,7 +183,7 @@ def run_reference(args):
                "path": "reference CPU path stand-in: numpy fp32 matmul of bf16-exact inputs (scripts/smoke.py:41)"},
     "cpu_baseline": {"value": round(tflops, 4), "unit": "TFLOPS", "cores": cores, "kind": "port", "sample": sample},
     "e2e": {"value": round(tflops, 4), "unit": "TFLOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-    "gpu_launches": 0}), flush=True)
+    "gpu_launches": 0})
 
 
 # ------------------------------------------------------------------------------------------------------------------
@@ -337,7 +338,7 @@ def run_ours(args):
     dist.destroy_process_group()
   if rank != 0: return
   tag = f"sm100_gemm_ws_{'pair' if info['paired'] else 'cta'}_{'tmast' if cfg.tma_store else 'reg'}"
-  traffic = profiled_traffic(tag, flops_rank)
+  traffic = profiled_traffic(tag, args.workload, flops_rank)
   line = {
     "metric": METRIC, "value": round(value, 3), "unit": "TFLOPS", "n_gpus": world, "steps": args.steps,
     "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": True, "scaling": scaling,
@@ -356,10 +357,23 @@ def run_ours(args):
     "parity": {"rel_err_vs_cublas": rel, "nan_after_poison": nan},
     "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": args.steps, "clocks": clocks.summary(),
   }
-  print(json.dumps(line), flush=True)
+  emit(line)
+
+
+_JSON_OUT = None
+
+
+def emit(line: dict) -> None:
+  """Print the result line on the real stdout (everything else that writes to stdout goes to stderr)."""
+  print(json.dumps(line), file=_JSON_OUT or sys.stdout, flush=True)
 
 
 def main():
+  global _JSON_OUT
+  # Keep stdout for the single JSON line: NCCL and other libraries print banners to fd 1, so fd 1 is pointed at
+  # stderr and the result goes through a private duplicate of the original stdout.
+  _JSON_OUT = os.fdopen(os.dup(1), "w")
+  os.dup2(2, 1)
   args = parse_args()
   if args.impl == "reference": run_reference(args)
   else: run_ours(args)
