@@ -56,6 +56,9 @@ enum {
  *               reads 25% fewer operand bytes per FLOP than 256 x 256 at the cost of a single TMEM accumulator
  *   no_tail_split   0 (default): when the persistent schedule's last wave is at most half full, its tiles are split
  *                   into half-width tiles so that the tail costs about half a tile; 1: keep whole tiles
+ *   ragged      0 (default): M, N, K must be multiples of the tile, as in the reference (gemm.py:303);
+ *               1 (persistent kernel): any M, and N, K multiples of 8 — edge tiles are zero-filled on load and clipped
+ *               or masked on store
  *   debug_skip_job  test hook: the producer never loads this job (-1 = off) so that the kernel's waits run out and
  *                   the launch reports an error instead of hanging
  */
@@ -76,7 +79,7 @@ typedef struct bg_cfg {
   int32_t debug_skip_job;
   int32_t n_mma;
   int32_t no_tail_split;
-  int32_t reserved;
+  int32_t ragged;
 } bg_cfg;
 
 /* What a plan resolved to (for reports and tests). */

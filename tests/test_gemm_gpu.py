@@ -247,3 +247,28 @@ def test_full_size_sampled(size, cfg_name, cuda_dev):
   cub = (A @ B).float()
   rel = float((C.float() - cub).abs().max() / (cub.abs().max() + 1e-9))
   assert rel <= TOL, rel
+
+
+# ------------------------------------------------------------------------------------------------------------------
+# shapes that are not tile multiples (opt-in WSCfg(ragged=True); the reference rejects them, gemm.py:303)
+# ------------------------------------------------------------------------------------------------------------------
+def _ragged_cases():
+  from hopper_wgmma import WSCfg
+  return [
+    ("pair_tmast_hilbert", WSCfg(tma_store=True, cluster=2, hilbert=True, ragged=True), (300, 520, 200)),
+    ("pair_regstore", WSCfg(cluster=2, ragged=True), (777, 1000, 1000)),
+    ("cta_tmast", WSCfg(BN=128, tma_store=True, ragged=True), (129, 136, 72)),
+    ("wide_pair", WSCfg(n_mma=2, cluster=2, tma_store=True, ragged=True), (1000, 1200, 328)),
+    ("bm64_reg_bn48", WSCfg(consumers=1, BN=48, ragged=True), (70, 104, 136)),
+    ("one_row", WSCfg(tma_store=True, ragged=True), (1, 264, 64)),
+    ("k8", WSCfg(cluster=2, tma_store=True, ragged=True), (256, 256, 8)),
+    ("exact_multiple", WSCfg(tma_store=True, cluster=2, ragged=True), (512, 512, 512)),
+  ]
+
+
+@pytest.mark.parametrize("idx", range(8))
+def test_ragged_shapes(idx, cuda_dev):
+  from hopper_wgmma import build_gemm_ws
+  name, cfg, (M, N, K) = _ragged_cases()[idx]
+  worst, launch = run_case(lambda: build_gemm_ws(N, cfg, M, K, wait_budget_ns=BUDGET_NS), M, N, K, cuda_dev)
+  assert worst <= TOL, f"{name} {M}x{N}x{K}: relative_error={worst:.5f} ({launch.info()['kernel']})"

@@ -228,3 +228,15 @@ def test_cpp_schedule_builders_reject_bad_sizes():
     _capi.grouped_order(4, 4, 5, 1)
   with pytest.raises(ValueError):
     _capi.hilbert_order(0, 4)
+
+
+def test_ragged_shape_contract():
+  from hopper_wgmma import WSCfg, build_gemm_ws
+  with pytest.raises(ValueError, match="not a multiple of tile"):
+    build_gemm_ws(500, WSCfg())
+  run = build_gemm_ws(520, WSCfg(ragged=True), 300, 200)
+  assert run.kernel_name.startswith("sm100_300x520x200")
+  with pytest.raises(ValueError, match="multiples of 8"):
+    build_gemm_ws(522, WSCfg(ragged=True), 300, 200)
+  with pytest.raises(ValueError, match="multiples of 8"):
+    build_gemm_ws(520, WSCfg(ragged=True), 300, 201)

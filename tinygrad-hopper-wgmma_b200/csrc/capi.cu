@@ -378,10 +378,19 @@ int32_t setup_plan(const bg_cfg& c, int64_t M, int64_t N, int64_t K, const void*
 
   // ---- shape contract (gemm.py:300-311)
   if (M <= 0 || N <= 0 || K <= 0) return fail(-1, "M, N and K must be positive");
-  if (M % bm || N % width || K % 64)
+  const bool ragged = c.ragged != 0;
+  if (ragged && c.kind != BG_KIND_WS) return fail(-1, "ragged shapes need the persistent kernel");
+  if (!ragged && (M % bm || N % width || K % 64))
     return fail(-1, "shape %lldx%lldx%lld not a multiple of tile %dx%dx64", (long long)M, (long long)N, (long long)K, bm,
                 width);
-  const int64_t mt = M / bm, nt = N / width, nkb = K / 64;
+  if (ragged && (N % 8 || K % 8))
+    return fail(-1, "ragged shapes need N and K to be multiples of 8 (16-byte rows), got N=%lld K=%lld", (long long)N,
+                (long long)K);
+  // Ragged shapes round the tile grid up: TMA loads zero-fill what lies beyond A, BT and K, the TMA store clips
+  // and the register epilogue masks what lies beyond C; a pair's second row tile may lie wholly outside A.
+  int64_t mt = (M + bm - 1) / bm;
+  const int64_t nt = (N + width - 1) / width, nkb = (K + 63) / 64;
+  if (ragged) mt = (mt + cl - 1) / cl * cl;
   if (mt % cl) return fail(-1, "%lld row tiles not divisible by cluster %d", (long long)mt, cl);
   const int64_t cmt = mt / cl;
   if (cmt > 0xFFFF || nt > 0xFFFF || cmt * nt > (1ll << 30) || nkb > (1ll << 30))
@@ -559,6 +568,8 @@ int32_t setup_plan(const bg_cfg& c, int64_t M, int64_t N, int64_t K, const void*
   kp.sched = nullptr;
   kp.C = static_cast<__nv_bfloat16*>(C);
   kp.ldc = ldc;
+  kp.m_valid = static_cast<int>(M);
+  kp.n_valid = static_cast<int>(N);
   kp.err = nullptr;
   kp.budget_ns = c.wait_budget_ns > 0 ? static_cast<unsigned long long>(c.wait_budget_ns) : 4000000000ull;
   kp.skip_job = c.debug_skip_job;

@@ -68,6 +68,8 @@ struct GemmParams {
                            // field marks a half-width tile whose column index counts half-width tiles
   __nv_bfloat16* C;        // output base (register epilogue)
   long long ldc;           // C row pitch in elements
+  int m_valid;             // rows of C (the register epilogue masks rows >= m_valid; the TMA store clips them)
+  int n_valid;             // columns of C (a multiple of 8; the same for columns)
   unsigned int* err;       // error word (0 = ok)
   unsigned long long budget_ns;  // per-wait time limit
   int skip_job;            // test hook: the producer never loads this job index (-1 = off); makes waits run out
@@ -106,21 +108,36 @@ __device__ __forceinline__ void store_row_global(__nv_bfloat16* dst, const uint3
                  pack_bf16x2(v[8 * j + 4], v[8 * j + 5]), pack_bf16x2(v[8 * j + 6], v[8 * j + 7]));
 }
 
+// Store the first `cols` (a multiple of 8) of N accumulator words as bf16; for tiles that overhang C's last column.
+template <int N>
+__device__ __forceinline__ void store_row_global_masked(__nv_bfloat16* dst, const uint32_t (&v)[N], int cols) {
+#pragma unroll
+  for (int j = 0; j < N / 8; ++j)
+    if (8 * j < cols)
+      st_global_v4(dst + 8 * j, pack_bf16x2(v[8 * j + 0], v[8 * j + 1]), pack_bf16x2(v[8 * j + 2], v[8 * j + 3]),
+                   pack_bf16x2(v[8 * j + 4], v[8 * j + 5]), pack_bf16x2(v[8 * j + 6], v[8 * j + 7]));
+}
+
 // Register epilogue for one accumulator: this thread's row, columns [0, bn), 32 at a time plus a 16-column tail.
-__device__ __forceinline__ void epilogue_registers(uint32_t tacc, __nv_bfloat16* crow, int bn, bool active) {
+// Only the first `cols` columns exist in C (cols >= bn for an interior tile); TMEM reads stay warp-uniform.
+__device__ __forceinline__ void epilogue_registers(uint32_t tacc, __nv_bfloat16* crow, int bn, bool active,
+                                                   int cols) {
   const int n32 = bn >> 5;
 #pragma unroll 1
   for (int c = 0; c < n32; ++c) {
     uint32_t v[32];
     tmem_ld_32x32b_x32(tacc + 32 * c, v);
     tmem_ld_wait();
-    if (active) store_row_global<32>(crow + 32 * c, v);
+    if (active) {
+      if (cols >= 32 * c + 32) store_row_global<32>(crow + 32 * c, v);
+      else if (cols > 32 * c) store_row_global_masked<32>(crow + 32 * c, v, cols - 32 * c);
+    }
   }
   if (bn & 16) {
     uint32_t v[16];
     tmem_ld_32x32b_x16(tacc + 32 * n32, v);
     tmem_ld_wait();
-    if (active) store_row_global<16>(crow + 32 * n32, v);
+    if (active && cols > 32 * n32) store_row_global_masked<16>(crow + 32 * n32, v, cols - 32 * n32);
   }
 }
 
@@ -370,7 +387,7 @@ __global__ void __launch_bounds__(kWsThreads, 1)
         }
       } else {
         __nv_bfloat16* crow = p.C + static_cast<long long>(row0 + lane) * p.ldc + col0;
-        epilogue_registers(tacc, crow, width, lane < ROWS_W);
+        epilogue_registers(tacc, crow, width, lane < ROWS_W && row0 + lane < p.m_valid, p.n_valid - col0);
       }
       tc_fence_before();
       __syncwarp();
@@ -507,7 +524,7 @@ __global__ void __launch_bounds__(kRingThreads, 1)
     const uint32_t tacc = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
     __nv_bfloat16* crow = p.C + static_cast<long long>(row_a + q * ROWS_W + lane) * p.ldc + row_b;
     // A failed tile leaves C unwritten (the host reports the error), but the TMEM reads stay warp-uniform.
-    epilogue_registers(tacc, crow, p.bn, ready && lane < ROWS_W);
+    epilogue_registers(tacc, crow, p.bn, ready && lane < ROWS_W, p.bn);
   }
 
   tc_fence_before();

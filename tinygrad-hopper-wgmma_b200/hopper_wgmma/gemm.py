@@ -143,6 +143,7 @@ class WSCfg:
   acc_bufs: int | None = None  # accumulator buffers in tensor memory; None = 2 when 2 * width <= 512 columns
   n_mma: int = 1               # tcgen05.mma instructions along N per K step: tiles are n_mma * BN columns wide
   split_tail: bool = True      # split a last wave that is at most half full into half-width tiles
+  ragged: bool = False         # accept any M (and N, K multiples of 8): edge tiles are zero-filled / clipped
 
   def __post_init__(self):
     if self.BK != 64: raise ValueError("BK must be 64 (one 128-byte swizzle atom)")
@@ -202,7 +203,7 @@ class WSCfg:
                        num_sm=num_sm or self.num_sm or 0, group_m=self.group_m, group_n=self.group_n,
                        tma_store=int(self.tma_store), cluster=self.cluster, hilbert=int(self.hilbert),
                        acc_bufs=self.acc_bufs or 0, wait_budget_ns=wait_budget_ns, debug_skip_job=debug_skip_job,
-                       n_mma=self.n_mma, no_tail_split=0 if self.split_tail else 1)
+                       n_mma=self.n_mma, no_tail_split=0 if self.split_tail else 1, ragged=int(self.ragged))
 
 
 # =============================================================================================================
@@ -247,8 +248,13 @@ def build_gemm_ws(N: int, cfg: WSCfg, M: int | None = None, K: int | None = None
   M, K = N if M is None else M, N if K is None else K
   if min(M, N, K) <= 0: raise ValueError("M, N and K must be positive")
   BM, BN, BK, CL = cfg.BM, cfg.width, cfg.BK, cfg.cluster
-  if M % BM or N % BN or K % BK: raise ValueError(f"shape {M}x{N}x{K} not a multiple of tile {BM}x{BN}x{BK}")
-  MT, NT = M // BM, N // BN
+  if cfg.ragged:
+    if N % 8 or K % 8: raise ValueError(f"ragged shapes need N and K to be multiples of 8, got N={N} K={K}")
+    MT, NT = -(-M // BM), -(-N // BN)
+    MT = -(-MT // CL) * CL
+  else:
+    if M % BM or N % BN or K % BK: raise ValueError(f"shape {M}x{N}x{K} not a multiple of tile {BM}x{BN}x{BK}")
+    MT, NT = M // BM, N // BN
   if MT % CL: raise ValueError(f"{MT} row tiles not divisible by cluster {CL}")
   CMT = MT // CL
   _, grouped_2d = grouped_tile_order(CMT, NT, min(max(cfg.group_m // CL, 1), CMT), min(cfg.group_n, NT))
