@@ -41,8 +41,19 @@ B200 = {
   "pair_wide": WSCfg(tma_store=True, cluster=2, n_mma=2),
   "pair_wide_hilbert": WSCfg(tma_store=True, cluster=2, n_mma=2, hilbert=True),
   "pair_n128": WSCfg(BN=128, tma_store=True, cluster=2, hilbert=True),
+  "pair_n192": WSCfg(BN=192, tma_store=True, cluster=2, hilbert=True),
   "pair_reg": WSCfg(cluster=2, hilbert=True),
+  "cta_n128": WSCfg(BN=128, tma_store=True, hilbert=True),
+  "cta_n64": WSCfg(BN=64, tma_store=True, hilbert=True),
+  "m64_n128": WSCfg(consumers=1, BN=128, tma_store=True, hilbert=True),
 }
+
+# The shape sweep of the benchmark configuration (12 tile-multiple shapes) and the configs tried on each.
+SWEEP_SHAPES = [(512, 512, 512), (1024, 1024, 1024), (1536, 1536, 1536), (2048, 2048, 2048), (3072, 3072, 3072),
+                (6144, 6144, 6144), (12288, 12288, 12288), (16384, 16384, 16384), (16384, 4096, 4096),
+                (4096, 16384, 4096), (8192, 8192, 2048), (2048, 2048, 16384)]
+SWEEP_CONFIGS = ["cluster_hilbert", "hilbert", "pair_wide_hilbert", "pair_n128", "pair_n192", "cta_n128", "cta_n64",
+                 "m64_n128", "hilbert_n192"]
 
 # One-off comparisons quoted by the reference (all SMs vs 128 on an H200); here: 128 CTAs vs the device count.
 EXTRA = {

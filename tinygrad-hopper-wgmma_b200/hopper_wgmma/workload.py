@@ -88,7 +88,7 @@ def main(argv=None) -> int:
   a = torch.randn((M, K), generator=g, device=dev).to(torch.bfloat16)
   b = torch.randn((K, N), generator=g, device=dev).to(torch.bfloat16)
   c = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
-  flush = torch.empty(64 << 20, dtype=torch.int32, device=dev) if args.flush else None
+  flush = torch.empty(64 << 20, dtype=torch.int32, device=dev) if args.flush else None   # 256 MiB
   flops = 2.0 * M * N * K
   ref = (a @ b).float() if (args.check or args.torch) else None
   cub_us = None
