@@ -342,6 +342,26 @@ def run_ours(args):
                    "two streams, two buffer sets, steps overlapped",
            "steps": e2e_steps, "ms_per_step": round(e2e_ms / e2e_steps, 4)}
 
+  # Optional NCCL all-gather of the C shards over NVLink (A replicated, B and C column-sharded): timed separately,
+  # never inside the GEMM. Every rank runs the same collectives in the same order.
+  allgather = None
+  if world > 1:
+    for _ in range(3): shard.gather_columns(C, world, as_row_major=False)
+    torch.cuda.synchronize()
+    barrier()
+    ag_steps = 10
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for _ in range(ag_steps): shard.gather_columns(C, world, as_row_major=False)
+    ev1.record()
+    torch.cuda.synchronize()
+    ag_ms = shard.max_over_ranks(ev0.elapsed_time(ev1) / ag_steps, device=dev)
+    total_bytes = 2 * M * n * world
+    allgather = {"ms": round(ag_ms, 4), "bytes_gathered": total_bytes,
+                 "algbw_gbs": round(total_bytes / (ag_ms * 1e-3) / 1e9, 1),
+                 "busbw_gbs": round(total_bytes * (world - 1) / world / (ag_ms * 1e-3) / 1e9, 1),
+                 "what": "torch.distributed.all_gather_into_tensor (NCCL) of the bf16 C shards -> [world, M, N/world]"}
+
   cpu = None
   if rank == 0 and world == 1 and not args.no_cpu_baseline:
     tf, reps, secs = cpu_gemm_tflops(2048, 2048, 2048, CPU_SAMPLE_SECONDS, reps_min=2)
@@ -371,6 +391,7 @@ def run_ours(args):
                "kernel": "torch.matmul (cuBLAS), same inputs, same flush protocol, alternating with ours"},
     "parity": {"rel_err_vs_cublas": rel, "nan_after_poison": nan},
     "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": args.steps, "clocks": clocks.summary(),
+    "allgather_c": allgather,
   }
   emit(line)
 

@@ -118,13 +118,19 @@ def _b200_cases():
     ("tail_split_pair", WSCfg(tma_store=True, cluster=2, hilbert=True, num_sm=18), (1024, 1792, 128)),
     ("tail_split_wide_pair", WSCfg(n_mma=2, cluster=2, tma_store=True, num_sm=10), (1024, 1536, 128)),
     ("tail_split_bm64_reg", WSCfg(consumers=1, BN=128, num_sm=7), (320, 384, 128)),
+    ("wide_split_abc", WSCfg(n_mma=2, cluster=2, tma_store=True, split_tail=False), (512, 1024, 1024)),
+    ("wide_split_all_phase_a", WSCfg(n_mma=2, cluster=2, tma_store=True, split_tail=False), (512, 1024, 128)),
+    ("wide_split_no_phase_b", WSCfg(n_mma=2, cluster=2, tma_store=True, split_tail=False), (512, 1024, 192)),
+    ("wide_split_many_tiles", WSCfg(n_mma=2, cluster=2, tma_store=True, hilbert=True, num_sm=6), (1024, 2048, 320)),
+    ("wide_split_regstore", WSCfg(n_mma=2, cluster=2, split_tail=False), (256, 1024, 448)),
+    ("wide_split_cta", WSCfg(n_mma=2, tma_store=True, split_tail=False, num_sm=3), (384, 1536, 256)),
     ("gated_c1", GatedCfg(consumers=1, BN=128), (512, 512, 512)),
     ("ring_bn256", GatedCfg(consumers=0, BN=256, stages=2), (256, 256, 256)),
     ("ring_bn64", GatedCfg(consumers=0, BN=64, stages=3), (192, 192, 192)),
   ]
 
 
-@pytest.mark.parametrize("idx", range(28))
+@pytest.mark.parametrize("idx", range(34))
 def test_b200_cases(idx, cuda_dev):
   from hopper_wgmma.ladder import build
   name, cfg, (M, N, K) = _b200_cases()[idx]

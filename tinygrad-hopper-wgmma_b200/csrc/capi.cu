@@ -350,7 +350,7 @@ namespace {
 // its `sched` and `err` pointers, which the caller points at device memory of its own.
 int32_t setup_plan(const bg_cfg& c, int64_t M, int64_t N, int64_t K, const void* A, int64_t lda, const void* BT,
                    int64_t ldb, void* C, int64_t ldc, int32_t device, bg_plan* p, std::vector<int32_t>& sched,
-                   std::array<int, 8>& sched_key) {
+                   std::array<int, 8>& sched_key, bool validate_only = false) {
   // ---- knob validation (gemm.py:260-271, gated.py:27-32)
   if (c.kind != BG_KIND_WS && c.kind != BG_KIND_GATED && c.kind != BG_KIND_RING)
     return fail(-1, "unknown kernel kind %d", c.kind);
@@ -401,6 +401,8 @@ int32_t setup_plan(const bg_cfg& c, int64_t M, int64_t N, int64_t K, const void*
   if (lda < K || ldb < K || ldc < N || lda % 8 || ldb % 8 || ldc % 8)
     return fail(-1, "row pitches must cover the row and be multiples of 8 elements (lda=%lld ldb=%lld ldc=%lld)",
                 (long long)lda, (long long)ldb, (long long)ldc);
+
+  if (validate_only) return 0;   // the argument checks above touch no device
 
   int sm_count = 0, smem_optin = 0, ccmaj = 0, ccmin = 0;
   int32_t st = bg_device_info(device, &sm_count, &smem_optin, &ccmaj, &ccmin);
@@ -573,6 +575,9 @@ int32_t setup_plan(const bg_cfg& c, int64_t M, int64_t N, int64_t K, const void*
   kp.err = nullptr;
   kp.budget_ns = c.wait_budget_ns > 0 ? static_cast<unsigned long long>(c.wait_budget_ns) : 4000000000ull;
   kp.skip_job = c.debug_skip_job;
+  // split accumulator (two N blocks, one 512-column buffer): how many k-blocks run on half 0 alone at a tile's start
+  // and end; it must stay below the ring depth so the producer keeps a free stage
+  kp.look = std::max(1, std::min(2, stages - 2));
 
   snprintf(p->name, sizeof(p->name), "%s<BM=%d,%s,%s> BN=%dx%d stages=%d acc=%d tail=%d", c.kind == BG_KIND_RING ? "sm100_gemm_ring" : "sm100_gemm_ws",
            bm, paired ? "pair" : (cl == 2 ? "cluster2" : "cta"), p->tma_store ? "tma_store" : "reg_store", bn, nblk,
@@ -589,11 +594,13 @@ int32_t bg_plan_create(bg_plan** out, const bg_cfg* cfg, int64_t M, int64_t N, i
   if (out == nullptr || cfg == nullptr) return fail(-1, "null plan or cfg pointer");
   *out = nullptr;
   std::unique_ptr<bg_plan, void (*)(bg_plan*)> p(new bg_plan, free_plan);
-  DeviceGuard guard(device);
-  if (guard.status != cudaSuccess) return cuda_fail(guard.status, "cudaSetDevice");
   std::vector<int32_t> sched;
   std::array<int, 8> sched_key{};
-  int32_t st = setup_plan(*cfg, M, N, K, A, lda, BT, ldb, C, ldc, device, p.get(), sched, sched_key);
+  int32_t st = setup_plan(*cfg, M, N, K, A, lda, BT, ldb, C, ldc, device, p.get(), sched, sched_key, true);
+  if (st) return st;
+  DeviceGuard guard(device);
+  if (guard.status != cudaSuccess) return cuda_fail(guard.status, "cudaSetDevice");
+  st = setup_plan(*cfg, M, N, K, A, lda, BT, ldb, C, ldc, device, p.get(), sched, sched_key);
   if (st) return st;
   // ---- device buffers: tile table (cached per schedule) and error word (from the device's slab)
   if (!sched.empty() && (st = store_table(device, sched_key, sched, &p->d_sched))) return st;
@@ -641,12 +648,14 @@ int32_t bg_gemm_noalloc(const bg_cfg* cfg, int64_t M, int64_t N, int64_t K, cons
                         uint32_t* err_word) {
   if (cfg == nullptr) return fail(-1, "null cfg pointer");
   if (device < 0 || device >= 64) return fail(-1, "device %d out of range", device);
-  DeviceGuard guard(device);
-  if (guard.status != cudaSuccess) return cuda_fail(guard.status, "cudaSetDevice");
   bg_plan plan;   // lives on this stack frame and owns no device memory
   std::vector<int32_t> sched;
   std::array<int, 8> sched_key{};
-  int32_t st = setup_plan(*cfg, M, N, K, A, lda, BT, ldb, C, ldc, device, &plan, sched, sched_key);
+  int32_t st = setup_plan(*cfg, M, N, K, A, lda, BT, ldb, C, ldc, device, &plan, sched, sched_key, true);
+  if (st) return st;
+  DeviceGuard guard(device);
+  if (guard.status != cudaSuccess) return cuda_fail(guard.status, "cudaSetDevice");
+  st = setup_plan(*cfg, M, N, K, A, lda, BT, ldb, C, ldc, device, &plan, sched, sched_key);
   if (st) return st;
   if (sched.size() > static_cast<size_t>(kNoAllocMaxTiles))
     return fail(-1, "bg_gemm_noalloc: %zu tiles exceed its fixed scratch of %d tile entries; use bg_plan_create or "

@@ -72,6 +72,7 @@ struct GemmParams {
   int n_valid;             // columns of C (a multiple of 8; the same for columns)
   unsigned int* err;       // error word (0 = ok)
   unsigned long long budget_ns;  // per-wait time limit
+  int look;                // split accumulator: k-blocks of the half-0-first phases at tile start and end (< stages)
   int skip_job;            // test hook: the producer never loads this job index (-1 = off); makes waits run out
 };
 
@@ -272,6 +273,56 @@ __global__ void __launch_bounds__(kWsThreads, 1)
       uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
       int job = 0;
       bool failed = false;
+      // Two N blocks sharing one 512-column accumulator ("split" mode): each half of TMEM has its own full/empty
+      // barrier pair (the two pairs that otherwise serve two accumulator buffers), so the epilogue drains half 0
+      // while the MMAs of half 1 still run, and the next tile starts on half 0 while the epilogue drains half 1.
+      const bool split = NB == 2 && p.acc_bufs == 1;
+      auto adv = [&](uint32_t& st, uint32_t& ph) {
+        if (++st == static_cast<uint32_t>(p.stages)) {
+          st = 0;
+          ph ^= 1u;
+        }
+      };
+      auto issue = [&](uint32_t st, int kb, int nb_lo, int nb_hi, uint32_t d, uint32_t idesc) {
+        if (elect_one()) {
+          const uint64_t ad = smem_desc_sw128(sA + st * p.a_stage_bytes);
+          const uint64_t bd = smem_desc_sw128(sB + st * p.b_stage_bytes);
+          // +32 bytes along K inside the swizzle row = +2 in the descriptor's address field; N block nb reads the
+          // nb-th B sub-tile and accumulates into TMEM columns [nb * bn, (nb + 1) * bn)
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k)
+#pragma unroll
+            for (int nb = 0; nb < NB; ++nb)
+              if (nb >= nb_lo && nb < nb_hi)
+                mma_bf16<CG>(d + static_cast<uint32_t>(nb * p.bn), ad + 2u * k,
+                             bd + static_cast<uint64_t>((nb * p.b_block_bytes) >> 4) + 2u * k, idesc,
+                             (kb | k) != 0 ? 1u : 0u);
+        }
+        __syncwarp();
+      };
+      auto commit_both = [&](uint32_t bar) {   // arrive on this CTA's barrier and, in a pair, on the peer's
+        if (elect_one()) {
+          mma_commit<CG>(bar);
+          if (PAIRED) mma_commit<CG>(mapa_shared(bar, 1));
+        }
+        __syncwarp();
+      };
+      auto wait_full = [&](uint32_t st, uint32_t ph, int j) {
+        if (!mbar_wait_warp(full0 + 8u * st, ph, budget)) {
+          if (lane == 0) record_error(p.err, kErrMmaFull, j);
+          return false;
+        }
+        tc_fence_after();
+        return true;
+      };
+      auto wait_acc = [&](uint32_t bar, uint32_t parity, int i) {
+        if (!mbar_wait_warp(bar, parity, budget)) {
+          if (lane == 0) record_error(p.err, kErrMmaAcc, i);
+          return false;
+        }
+        tc_fence_after();
+        return true;
+      };
       for (int i = 0; !failed; ++i) {
         const int idx = cid + i * p.nclusters;
         if (idx >= p.tiles) break;
@@ -280,51 +331,110 @@ __global__ void __launch_bounds__(kWsThreads, 1)
         tile_coords(p, idx, cm, tn, narrow);
         const int nblk = (narrow && NB == 2) ? 1 : NB;
         const uint32_t idesc = (narrow && NB == 1) ? p.idesc_narrow : p.idesc;
-        if (!mbar_wait_warp(tempty0 + 8u * acc, acc_phase ^ 1u, budget)) {
-          if (lane == 0) record_error(p.err, kErrMmaAcc, i);
-          break;
+        const int nk = p.num_kb;
+        if (!split) {
+          if (!wait_acc(tempty0 + 8u * acc, acc_phase ^ 1u, i)) break;
+          const uint32_t d = tmem_base + acc * static_cast<uint32_t>(p.acc_stride);
+          for (int kb = 0; kb < nk; ++kb, ++job) {
+            if (!wait_full(stage, phase, job)) {
+              failed = true;
+              break;
+            }
+            issue(stage, kb, 0, nblk, d, idesc);
+            commit_both(empty0 + 8u * stage);
+            adv(stage, phase);
+          }
+          if (failed) break;
+          commit_both(tfull0 + 8u * acc);
+          if (++acc == static_cast<uint32_t>(p.acc_bufs)) {
+            acc = 0;
+            acc_phase ^= 1u;
+          }
+          continue;
         }
-        tc_fence_after();
-        const uint32_t d = tmem_base + acc * static_cast<uint32_t>(p.acc_stride);
-        for (int kb = 0; kb < p.num_kb; ++kb, ++job) {
-          if (!mbar_wait_warp(full0 + 8u * stage, phase, budget)) {
-            if (lane == 0) record_error(p.err, kErrMmaFull, job);
+        // split mode: tile i uses TMEM half h through tfull0/tempty0 + 8h, parity acc_phase (flips per tile)
+        const uint32_t d = tmem_base;
+        if (nblk == 1) {
+          // a half-width tail tile: half 0 only, streamed like the unsplit path; half 1's barriers still take one
+          // phase per tile so that both sides stay in step
+          if (!wait_acc(tempty0, acc_phase ^ 1u, i)) break;
+          for (int kb = 0; kb < nk; ++kb, ++job) {
+            if (!wait_full(stage, phase, job)) {
+              failed = true;
+              break;
+            }
+            issue(stage, kb, 0, 1, d, idesc);
+            commit_both(empty0 + 8u * stage);
+            adv(stage, phase);
+          }
+          if (failed) break;
+          commit_both(tfull0);
+          if (!wait_acc(tempty0 + 8u, acc_phase ^ 1u, i)) break;
+          commit_both(tfull0 + 8u);
+          acc_phase ^= 1u;
+          continue;
+        }
+        const int la = nk < p.look ? nk : p.look;                 // phase A k-blocks [0, la)
+        const int lc = (nk - la) < p.look ? nk - la : p.look;     // phase C k-blocks [nk - lc, nk)
+        // phase A: half 0 of k-blocks [0, la) as soon as half 0 is free (holding those la < stages stages), then
+        // half 1 of the same k-blocks once half 1 is free, releasing each stage
+        if (!wait_acc(tempty0, acc_phase ^ 1u, i)) break;
+        uint32_t st = stage, ph = phase;
+        for (int kb = 0; kb < la; ++kb) {
+          if (!wait_full(st, ph, job + kb)) {
             failed = true;
             break;
           }
-          tc_fence_after();
-          if (elect_one()) {
-            const uint64_t ad = smem_desc_sw128(sA + stage * p.a_stage_bytes);
-            const uint64_t bd = smem_desc_sw128(sB + stage * p.b_stage_bytes);
-            // +32 bytes along K inside the swizzle row = +2 in the descriptor's address field; N block nb reads the
-            // nb-th B sub-tile and accumulates into TMEM columns [nb * bn, (nb + 1) * bn)
-#pragma unroll
-            for (int k = 0; k < kBK / 16; ++k)
-#pragma unroll
-              for (int nb = 0; nb < NB; ++nb)
-                if (nb < nblk)
-                  mma_bf16<CG>(d + static_cast<uint32_t>(nb * p.bn), ad + 2u * k,
-                               bd + static_cast<uint64_t>((nb * p.b_block_bytes) >> 4) + 2u * k, idesc,
-                               (kb | k) != 0 ? 1u : 0u);
-            mma_commit<CG>(empty0 + 8u * stage);
-            if (PAIRED) mma_commit<CG>(mapa_shared(empty0 + 8u * stage, 1));
-          }
-          __syncwarp();
-          if (++stage == static_cast<uint32_t>(p.stages)) {
-            stage = 0;
-            phase ^= 1u;
-          }
+          issue(st, kb, 0, 1, d, idesc);
+          adv(st, ph);
         }
         if (failed) break;
-        if (elect_one()) {
-          mma_commit<CG>(tfull0 + 8u * acc);
-          if (PAIRED) mma_commit<CG>(mapa_shared(tfull0 + 8u * acc, 1));
+        if (la == nk) commit_both(tfull0);   // the whole tile was phase A: half 0 is complete
+        if (!wait_acc(tempty0 + 8u, acc_phase ^ 1u, i)) break;
+        st = stage;
+        ph = phase;
+        for (int kb = 0; kb < la; ++kb) {
+          issue(st, kb, 1, 2, d, idesc);
+          commit_both(empty0 + 8u * st);
+          adv(st, ph);
         }
-        __syncwarp();
-        if (++acc == static_cast<uint32_t>(p.acc_bufs)) {
-          acc = 0;
-          acc_phase ^= 1u;
+        if (la < nk) {
+          // phase B: both halves per k-block
+          for (int kb = la; kb < nk - lc; ++kb) {
+            if (!wait_full(st, ph, job + kb)) {
+              failed = true;
+              break;
+            }
+            issue(st, kb, 0, 2, d, idesc);
+            commit_both(empty0 + 8u * st);
+            adv(st, ph);
+          }
+          if (failed) break;
+          // phase C: half 0 of the last lc k-blocks (holding lc < stages stages), publish half 0, then half 1
+          const uint32_t st_c = st, ph_c = ph;
+          for (int kb = nk - lc; kb < nk; ++kb) {
+            if (!wait_full(st, ph, job + kb)) {
+              failed = true;
+              break;
+            }
+            issue(st, kb, 0, 1, d, idesc);
+            adv(st, ph);
+          }
+          if (failed) break;
+          commit_both(tfull0);
+          st = st_c;
+          ph = ph_c;
+          for (int kb = nk - lc; kb < nk; ++kb) {
+            issue(st, kb, 1, 2, d, idesc);
+            commit_both(empty0 + 8u * st);
+            adv(st, ph);
+          }
         }
+        commit_both(tfull0 + 8u);
+        stage = st;
+        phase = ph;
+        job += nk;
+        acc_phase ^= 1u;
       }
       if (elect_one()) mma_commit<CG>(drain);   // every MMA issued above has finished once this arrives
       __syncwarp();
@@ -336,24 +446,13 @@ __global__ void __launch_bounds__(kWsThreads, 1)
     const int q = warp & 3;   // TMEM lane quadrant this warp may access
     const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
     const uint32_t my_stage = sC + static_cast<uint32_t>(q) * 2u * STAGE_C;
+    const bool split = NB == 2 && p.acc_bufs == 1;
     uint32_t acc = 0, acc_phase = 0, chunk = 0;
-    for (int i = 0;; ++i) {
-      const int idx = cid + i * p.nclusters;
-      if (idx >= p.tiles) break;
-      int cm, tn;
-      bool narrow;
-      tile_coords(p, idx, cm, tn, narrow);
-      const int row0 = (cm * p.cl + static_cast<int>(rank)) * BM + q * ROWS_W;   // first row of this warp
-      const int width = narrow ? p.bn * NB / 2 : p.bn * NB;   // output columns of this tile
-      const int col0 = tn * width;
-      if (!mbar_wait_warp(tfull0 + 8u * acc, acc_phase, budget)) {
-        record_error(p.err, kErrEpilogue, i);
-        break;
-      }
-      tc_fence_after();
-      const uint32_t tacc = tmem_base + lane_base + acc * static_cast<uint32_t>(p.acc_stride);
+    // Write accumulator columns starting at TMEM address tacc (this warp's lanes) to C rows row0.., columns
+    // [ccol, ccol + ncols).
+    auto drain = [&](uint32_t tacc, int row0, int ccol, int ncols) {
       if constexpr (TMA_STORE) {
-        const int nchunks = width >> 6;
+        const int nchunks = ncols >> 6;
 #pragma unroll 1
         for (int c = 0; c < nchunks; ++c, ++chunk) {
           uint32_t v0[32], v1[32];
@@ -381,28 +480,67 @@ __global__ void __launch_bounds__(kWsThreads, 1)
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) {
-            tma_store_2d(&tmC, buf, col0 + 64 * c, row0);
+            tma_store_2d(&tmC, buf, ccol + 64 * c, row0);
             bulk_commit_group();
           }
         }
       } else {
-        __nv_bfloat16* crow = p.C + static_cast<long long>(row0 + lane) * p.ldc + col0;
-        epilogue_registers(tacc, crow, width, lane < ROWS_W && row0 + lane < p.m_valid, p.n_valid - col0);
+        __nv_bfloat16* crow = p.C + static_cast<long long>(row0 + lane) * p.ldc + ccol;
+        epilogue_registers(tacc, crow, ncols, lane < ROWS_W && row0 + lane < p.m_valid, p.n_valid - ccol);
       }
+    };
+    auto release = [&](uint32_t bar) {
       tc_fence_before();
       __syncwarp();
       if (lane == 0) {
         if (PAIRED)
-          mbar_arrive_cluster(mapa_shared(tempty0 + 8u * acc, 0));
+          mbar_arrive_cluster(mapa_shared(bar, 0));
         else
-          mbar_arrive_local(tempty0 + 8u * acc);
+          mbar_arrive_local(bar);
       }
+    };
+    for (int i = 0;; ++i) {
+      const int idx = cid + i * p.nclusters;
+      if (idx >= p.tiles) break;
+      int cm, tn;
+      bool narrow;
+      tile_coords(p, idx, cm, tn, narrow);
+      const int row0 = (cm * p.cl + static_cast<int>(rank)) * BM + q * ROWS_W;   // first row of this warp
+      const int width = narrow ? p.bn * NB / 2 : p.bn * NB;   // output columns of this tile
+      const int col0 = tn * width;
+      if (split) {
+        // half h = TMEM columns [h * bn, (h + 1) * bn) with its own barriers; a half-width tile has only half 0
+        bool ok = true;
+        for (int h = 0; h < 2; ++h) {
+          if (!mbar_wait_warp(tfull0 + 8u * h, acc_phase, budget)) {
+            record_error(p.err, kErrEpilogue, i);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          if (h == 0 || !narrow)
+            drain(tmem_base + lane_base + static_cast<uint32_t>(h * p.bn), row0, col0 + h * p.bn, p.bn);
+          release(tempty0 + 8u * h);
+        }
+        if (!ok) break;
+        acc_phase ^= 1u;
+        continue;
+      }
+      if (!mbar_wait_warp(tfull0 + 8u * acc, acc_phase, budget)) {
+        record_error(p.err, kErrEpilogue, i);
+        break;
+      }
+      tc_fence_after();
+      drain(tmem_base + lane_base + acc * static_cast<uint32_t>(p.acc_stride), row0, col0, width);
+      release(tempty0 + 8u * acc);
       if (++acc == static_cast<uint32_t>(p.acc_bufs)) {
         acc = 0;
         acc_phase ^= 1u;
       }
     }
-    if (TMA_STORE && lane == 0) bulk_wait_group<0>();
+    // Shared memory must outlive the TMA engine's reads of the staging buffers; the global writes themselves are
+    // complete when the grid is.
+    if (TMA_STORE && lane == 0) bulk_wait_group_read<0>();
     __syncwarp();
   }
 

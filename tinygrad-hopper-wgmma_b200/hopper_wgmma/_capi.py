@@ -108,6 +108,7 @@ class Plan:
                ldc: int, device: int):
     self._h = ctypes.c_void_p()
     self._cfg = cfg
+    self._destroy = LIB.bg_plan_destroy   # kept on the instance: module globals may be gone when __del__ runs at exit
     check(LIB.bg_plan_create(ctypes.byref(self._h), ctypes.byref(cfg), M, N, K, a_ptr, lda, bt_ptr, ldb, c_ptr, ldc,
                              device), "bg_plan_create")
     self.device = device
@@ -132,5 +133,5 @@ class Plan:
   def __del__(self):
     h = getattr(self, "_h", None)
     if h is not None and h.value:
-      LIB.bg_plan_destroy(h)
+      self._destroy(h)
       self._h = ctypes.c_void_p()
