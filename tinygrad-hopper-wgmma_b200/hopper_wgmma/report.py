@@ -31,14 +31,15 @@ def _time_lines(text: str):
 def sweep(reps: int, out) -> None:
   from . import workload
   from .ladder import LADDER, SWEEP_CONFIGS, SWEEP_SHAPES
-  jobs = [((4096, 4096, 4096), list(LADDER)), ((8192, 8192, 8192), list(LADDER))]
+  ladder = list(LADDER) + ["pair_wide_hilbert"]   # the reference's rungs, plus B200's wide pair tiles
+  jobs = [((4096, 4096, 4096), ladder), ((8192, 8192, 8192), ladder)]
   jobs += [(shape, SWEEP_CONFIGS) for shape in SWEEP_SHAPES]
   for (m, n, k), names in jobs:
     buf = io.StringIO()
     with contextlib.redirect_stdout(buf):
       workload.main(["--shape", f"{m}x{n}x{k}", "--configs", ",".join(names), "--reps", str(reps), "--torch",
                      "--check", "--time", "--flush"])
-    tag = "ladder" if names == list(LADDER) else "sweep"
+    tag = "ladder" if set(LADDER) <= set(names) else "sweep"
     for line in buf.getvalue().splitlines():
       if line.startswith(("TIME ", "CHECK ", "SKIP ")):
         print(f"{line} " if line.startswith("TIME ") else line, file=out, flush=True)
@@ -58,7 +59,8 @@ def ncu_sweep(reps: int, out, jobs=None) -> None:
   from . import ncu_table
   from .ladder import LADDER, SWEEP_CONFIGS, SWEEP_SHAPES
   if jobs is None:
-    jobs = [((4096, 4096, 4096), list(LADDER)), ((8192, 8192, 8192), list(LADDER))]
+    ladder = list(LADDER) + ["pair_wide_hilbert"]   # the reference's rungs, plus B200's wide pair tiles
+    jobs = [((4096, 4096, 4096), ladder), ((8192, 8192, 8192), ladder)]
     jobs += [(shape, SWEEP_CONFIGS) for shape in SWEEP_SHAPES]
   env = dict(os.environ, PYTHONPATH=str(Path(__file__).resolve().parents[1]))
   for (m, n, k), names in jobs:
