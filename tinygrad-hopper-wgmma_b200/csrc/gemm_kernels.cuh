@@ -17,6 +17,10 @@
 //                    reads fp32 columns with tcgen05.ld, rounds to bf16 and writes C either directly
 //                    (register epilogue) or through a 128B-swizzled staging buffer and a TMA store (per warp,
 //                    double-buffered), then frees the accumulator buffer for the next tile.
+// With two N blocks per tile and one 512-column accumulator (NB == 2, acc_bufs == 1) the accumulator is split in two
+// 256-column halves with their own full/empty barriers: the MMA warp issues the half-0 MMAs of a tile's last k-blocks
+// first and publishes half 0, so the epilogue drains it while half 1 finishes, and starts the next tile on half 0
+// while the epilogue drains half 1.
 // In a CTA pair (PAIRED, cta_group::2) both CTAs load their own A rows and their own half of the B tile; only the
 // even CTA issues MMAs (M = 256 across the pair); the odd CTA's loads complete on the even CTA's barriers and the
 // MMA commits arrive on both CTAs' barriers. No load is multicast.
