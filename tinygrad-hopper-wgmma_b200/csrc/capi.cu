@@ -578,6 +578,8 @@ int32_t setup_plan(const bg_cfg& c, int64_t M, int64_t N, int64_t K, const void*
   // split accumulator (two N blocks, one 512-column buffer): how many k-blocks run on half 0 alone at a tile's start
   // and end; it must stay below the ring depth so the producer keeps a free stage
   kp.look = std::max(1, std::min(2, stages - 2));
+  // the first wave of the tile table also travels in the kernel parameters (see FirstTile in the kernel)
+  for (size_t i = 0; i < sched.size() && i < static_cast<size_t>(sm100::kFirstWave); ++i) kp.first_wave[i] = sched[i];
 
   snprintf(p->name, sizeof(p->name), "%s<BM=%d,%s,%s> BN=%dx%d stages=%d acc=%d tail=%d", c.kind == BG_KIND_RING ? "sm100_gemm_ring" : "sm100_gemm_ws",
            bm, paired ? "pair" : (cl == 2 ? "cluster2" : "cta"), p->tma_store ? "tma_store" : "reg_store", bn, nblk,

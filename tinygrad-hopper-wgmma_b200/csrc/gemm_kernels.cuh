@@ -36,6 +36,7 @@ namespace sm100 {
 constexpr int kBK = 64;           // K per pipeline stage: one 128-byte swizzle row of bf16
 constexpr int kWsThreads = 256;   // warps 0-3 producer / MMA / idle, warps 4-7 epilogue
 constexpr int kRingThreads = 128;
+constexpr int kFirstWave = 160;   // first-wave tile entries passed in the kernel parameters (>= clusters on a B200)
 
 // Error word layout: role in bits 24-31, the role's job or tile counter (saturated) in bits 0-23.
 enum : uint32_t {
@@ -78,6 +79,7 @@ struct GemmParams {
   unsigned long long budget_ns;  // per-wait time limit
   int look;                // split accumulator: k-blocks of the half-0-first phases at tile start and end (< stages)
   int skip_job;            // test hook: the producer never loads this job index (-1 = off); makes waits run out
+  int32_t first_wave[kFirstWave];  // sched[0 .. min(tiles, kFirstWave)) again, delivered with the launch
 };
 
 __device__ __forceinline__ void record_error(unsigned int* err, uint32_t role, uint32_t counter) {
@@ -103,6 +105,29 @@ __device__ __forceinline__ void tile_coords(const GemmParams& p, int idx, int& c
   bool narrow;
   tile_coords(p, idx, cm, tn, narrow);
 }
+
+// The first tile of a persistent cluster comes from the kernel parameters (a copy of the table's first wave), so the
+// first TMA load does not wait for a cold global-memory read of the tile table (about 1 us per launch, which matters
+// for microsecond-scale problems).
+struct FirstTile {
+  int idx = -1;
+  int entry = 0;
+  __device__ __forceinline__ void load(const GemmParams& p, int cid) {
+    if (p.sched != nullptr && cid < p.tiles && cid < kFirstWave) {
+      idx = cid;
+      entry = p.first_wave[cid];   // kernel-parameter space: no global-memory round trip before the first TMA
+    }
+  }
+  __device__ __forceinline__ void coords(const GemmParams& p, int i, int& cm, int& tn, bool& narrow) const {
+    if (i == idx) {
+      cm = entry >> 16;
+      tn = entry & 0x7FFF;
+      narrow = (entry & kNarrowTile) != 0;
+    } else {
+      tile_coords(p, i, cm, tn, narrow);
+    }
+  }
+};
 
 // Round 2N fp32 accumulator words to bf16 and store N/2 packed words per 16-byte chunk.
 template <int N>
@@ -150,7 +175,7 @@ template <int BM, bool PAIRED, bool TMA_STORE, int NB>
 __global__ void __launch_bounds__(kWsThreads, 1)
     sm100_gemm_ws(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                   const __grid_constant__ CUtensorMap tmBn, const __grid_constant__ CUtensorMap tmC,
-                  const GemmParams p) {
+                  const __grid_constant__ GemmParams p) {
   static_assert(BM == 64 || BM == 128, "BM is 64 or 128 rows per CTA");
   static_assert(!PAIRED || BM == 128, "CTA pairs use M = 256 (128 rows per CTA)");
   constexpr int CG = PAIRED ? 2 : 1;
@@ -178,6 +203,8 @@ __global__ void __launch_bounds__(kWsThreads, 1)
   const int cid = static_cast<int>(blockIdx.x) / p.cl;
   const bool leader = !PAIRED || rank == 0;
   const uint64_t budget = p.budget_ns;
+  FirstTile first;
+  first.load(p, cid);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < p.stages; ++s) {
@@ -217,7 +244,7 @@ __global__ void __launch_bounds__(kWsThreads, 1)
       if (idx >= p.tiles) break;
       int cm, tn;
       bool narrow;
-      tile_coords(p, idx, cm, tn, narrow);
+      first.coords(p, idx, cm, tn, narrow);
       // A half-width tile keeps NB == 2's MMA N and drops the second N block, or halves NB == 1's MMA N
       const int nblk = (narrow && NB == 2) ? 1 : NB;
       const CUtensorMap* mapB = (narrow && NB == 1) ? &tmBn : &tmB;
@@ -332,7 +359,7 @@ __global__ void __launch_bounds__(kWsThreads, 1)
         if (idx >= p.tiles) break;
         int cm, tn;
         bool narrow;
-        tile_coords(p, idx, cm, tn, narrow);
+        first.coords(p, idx, cm, tn, narrow);
         const int nblk = (narrow && NB == 2) ? 1 : NB;
         const uint32_t idesc = (narrow && NB == 1) ? p.idesc_narrow : p.idesc;
         const int nk = p.num_kb;
@@ -508,7 +535,7 @@ __global__ void __launch_bounds__(kWsThreads, 1)
       if (idx >= p.tiles) break;
       int cm, tn;
       bool narrow;
-      tile_coords(p, idx, cm, tn, narrow);
+      first.coords(p, idx, cm, tn, narrow);
       const int row0 = (cm * p.cl + static_cast<int>(rank)) * BM + q * ROWS_W;   // first row of this warp
       const int width = narrow ? p.bn * NB / 2 : p.bn * NB;   // output columns of this tile
       const int col0 = tn * width;
@@ -565,7 +592,7 @@ __global__ void __launch_bounds__(kWsThreads, 1)
 template <int BM>
 __global__ void __launch_bounds__(kRingThreads, 1)
     sm100_gemm_ring(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                    const GemmParams p) {
+                    const __grid_constant__ GemmParams p) {
   constexpr int ROWS_W = BM / 4;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
