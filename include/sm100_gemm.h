@@ -61,6 +61,14 @@ enum {
  *               or masked on store
  *   debug_skip_job  test hook: the producer never loads this job (-1 = off) so that the kernel's waits run out and
  *                   the launch reports an error instead of hanging
+ *   split_k     0 or 1: off. -1: automatic (the most splits, up to 16, that keep all tiles' splits within one wave of
+ *               clusters with at least 32 k-blocks each; off otherwise).
+ *               S in [2, 64] (persistent kernel, tiles a multiple of 32 columns wide, S <= K / 64):
+ *               each output tile is computed by S entries of the schedule, each over a contiguous 1/S of K, on
+ *               different clusters; every entry writes its fp32 partial sums to a plan-owned workspace and the
+ *               entry that finishes last adds them in split order (bitwise reproducible) and writes C; no entry
+ *               waits for another. For shapes with few tiles and long K. Not available through bg_gemm_noalloc (it
+ *               owns no workspace).
  */
 typedef struct bg_cfg {
   int32_t kind;
@@ -80,6 +88,7 @@ typedef struct bg_cfg {
   int32_t n_mma;
   int32_t no_tail_split;
   int32_t ragged;
+  int32_t split_k;
 } bg_cfg;
 
 /* What a plan resolved to (for reports and tests). */
@@ -98,6 +107,7 @@ typedef struct bg_plan_info {
   int32_t tmem_cols;      /* tensor-memory columns allocated per CTA         */
   int32_t max_active_clusters; /* occupancy limit reported by the runtime (0 if not queried) */
   int32_t narrow_tiles;   /* half-width tiles in the last wave (0 = no tail split)             */
+  int32_t split_k;        /* K splits per output tile (1 = off)                                */
   char kernel[96];        /* kernel family and template arguments            */
 } bg_plan_info;
 

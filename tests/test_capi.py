@@ -44,6 +44,11 @@ def _cfg(**kw):
   ({"kind": 2, "consumers": 0, "cluster": 2}, (512, 512, 512), "need the persistent kernel"),
   ({"kind": 2, "consumers": 2}, (512, 512, 512), "consumers == 0"),
   ({"kind": 7}, (512, 512, 512), "unknown kernel kind"),
+  ({"split_k": 65}, (512, 512, 4096 + 128), "split_k must be -1 (auto) or in [0, 64]"),
+  ({"split_k": -2}, (512, 512, 512), "split_k must be -1 (auto)"),
+  ({"split_k": 2, "kind": 1}, (512, 512, 512), "split_k needs the persistent kernel"),
+  ({"split_k": 9}, (512, 512, 512), "exceeds the 8 k-blocks"),
+  ({"split_k": 2, "BN": 48}, (512, 480, 512), "multiple of 32 columns"),
 ])
 def test_contract_violations_are_negative_status(kw, shape, msg):
   st, err = _create(_cfg(**kw), *shape)
@@ -90,3 +95,6 @@ def test_noalloc_entry_checks_arguments_first():
   assert st < 0 and "BN must be" in _capi.last_error()
   st = lib.bg_gemm_noalloc(None, 512, 512, 512, FAKE_A, 512, FAKE_B, 512, FAKE_C, 512, 0, None, None)
   assert st < 0
+  cfg = _cfg(split_k=2)
+  st = lib.bg_gemm_noalloc(ctypes.byref(cfg), 512, 512, 512, FAKE_A, 512, FAKE_B, 512, FAKE_C, 512, 0, None, None)
+  assert st < 0 and "split-K" in _capi.last_error()

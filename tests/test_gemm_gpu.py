@@ -278,3 +278,87 @@ def test_ragged_shapes(idx, cuda_dev):
   name, cfg, (M, N, K) = _ragged_cases()[idx]
   worst, launch = run_case(lambda: build_gemm_ws(N, cfg, M, K, wait_budget_ns=BUDGET_NS), M, N, K, cuda_dev)
   assert worst <= TOL, f"{name} {M}x{N}x{K}: relative_error={worst:.5f} ({launch.info()['kernel']})"
+
+
+# ------------------------------------------------------------------------------------------------------------------
+# split-K (WSCfg(split_k=S)): S entries per output tile over disjoint K ranges, reduced in-kernel by the last arrival
+# ------------------------------------------------------------------------------------------------------------------
+def _split_k_cases():
+  from hopper_wgmma import WSCfg
+  return [
+    ("cta_tmast_sk2", WSCfg(BN=128, tma_store=True, hilbert=True, split_k=2), (512, 512, 1024)),
+    ("cta_reg_sk3_uneven_k", WSCfg(BN=128, split_k=3), (256, 256, 448)),               # 7 k-blocks: 2 + 2 + 3
+    ("bm64_sk4", WSCfg(consumers=1, BN=128, tma_store=True, split_k=4), (256, 512, 512)),
+    ("pair_tmast_sk2", WSCfg(tma_store=True, cluster=2, hilbert=True, split_k=2), (512, 512, 512)),
+    ("pair_reg_sk4", WSCfg(cluster=2, split_k=4), (512, 512, 1024)),
+    ("wide_pair_sk2", WSCfg(n_mma=2, cluster=2, tma_store=True, split_k=2), (512, 1024, 1024)),
+    ("wide_pair_sk3_short", WSCfg(n_mma=2, cluster=2, tma_store=True, split_k=3), (512, 1024, 384)),
+    ("waves_sk2", WSCfg(BN=128, tma_store=True, hilbert=True, num_sm=6, split_k=2), (512, 640, 256)),
+    ("one_kblock_each_sk8", WSCfg(BN=64, tma_store=True, split_k=8), (128, 256, 512)),
+    ("ragged_pair_sk2", WSCfg(tma_store=True, cluster=2, ragged=True, split_k=2), (300, 520, 1000)),
+    ("pair_sk5_few_clusters", WSCfg(cluster=2, split_k=5, num_sm=8), (512, 256, 640)),
+  ]
+
+
+@pytest.mark.parametrize("idx", range(11))
+def test_split_k(idx, cuda_dev):
+  """Three launches of one plan on NaN-poisoned C: also checks that every launch leaves the arrival words zero."""
+  from hopper_wgmma import build_gemm_ws
+  name, cfg, (M, N, K) = _split_k_cases()[idx]
+  worst, launch = run_case(lambda: build_gemm_ws(N, cfg, M, K, wait_budget_ns=BUDGET_NS), M, N, K, cuda_dev)
+  info = launch.info()
+  assert info["split_k"] == cfg.split_k and f"splitk={cfg.split_k}" in info["kernel"]
+  assert worst <= TOL, f"{name} {M}x{N}x{K}: relative_error={worst:.5f} ({info['kernel']})"
+
+
+def test_split_k_is_bitwise_reproducible(cuda_dev):
+  """The last arrival adds the splits in split order whatever the arrival order, so repeated launches agree bit for
+  bit (while the splits race differently each time)."""
+  torch = _torch()
+  from hopper_wgmma import WSCfg, build_gemm_ws
+  M, N, K = 768, 768, 2048
+  a_bits, b_bits = inputs(M, N, K, seed=21)
+  A, B = to_dev(a_bits, cuda_dev), to_dev(b_bits, cuda_dev)
+  C = torch.empty((M, N), dtype=torch.bfloat16, device=cuda_dev)
+  launch = build_gemm_ws(N, WSCfg(BN=128, tma_store=True, split_k=4), M, K, wait_budget_ns=BUDGET_NS)(A, B, C)
+  outs = []
+  for _ in range(5):
+    poison(C)
+    launch()
+    launch.check()
+    outs.append(to_bits(C))
+  assert all((o == outs[0]).all() for o in outs[1:])
+
+
+def test_split_k_timeout_reports_error_and_plans_recover(cuda_dev):
+  """A split that never gets its operands: the other splits of its tile publish and leave (none of them is last),
+  the stuck one times out, the launch reports the error and the host clears the arrival words."""
+  torch = _torch()
+  from hopper_wgmma import WSCfg, build_gemm_ws
+  cfg = WSCfg(BN=128, tma_store=True, split_k=2)
+  M = N = K = 256
+  A = torch.zeros((M, K), dtype=torch.bfloat16, device=cuda_dev)
+  B = torch.zeros((K, N), dtype=torch.bfloat16, device=cuda_dev)
+  C = torch.empty((M, N), dtype=torch.bfloat16, device=cuda_dev)
+  bad = build_gemm_ws(N, cfg, M, K, wait_budget_ns=50_000_000, debug_skip_job=1)(A, B, C)
+  bad()
+  with pytest.raises(RuntimeError, match="timed out"):
+    bad.check()
+  worst, _ = run_case(lambda: build_gemm_ws(N, cfg, M, K, wait_budget_ns=BUDGET_NS), M, N, K, cuda_dev, reps=2)
+  assert worst <= TOL
+
+
+def test_split_k_auto_choice(cuda_dev):
+  """split_k=-1 splits only shapes with few tiles and long K: as many splits as keep one wave of clusters, each
+  with at least 32 k-blocks."""
+  from hopper_wgmma import WSCfg, build_gemm_ws
+  from hopper_wgmma._capi import device_info
+  sms = device_info(cuda_dev.index or 0)["sm_count"]
+  cfg = WSCfg(BN=64, tma_store=True, split_k=-1)
+  M, N, K = 256, 1024, 16384                      # 2 x 16 tiles of 128 x 64, 256 k-blocks
+  worst, launch = run_case(lambda: build_gemm_ws(N, cfg, M, K, wait_budget_ns=BUDGET_NS), M, N, K, cuda_dev, reps=2)
+  assert worst <= TOL
+  assert launch.info()["split_k"] == min(sms // 32, 8, 16)
+  _, launch = run_case(lambda: build_gemm_ws(1024, cfg, 1024, 1024, wait_budget_ns=BUDGET_NS), 1024, 1024, 1024,
+                       cuda_dev, reps=1)
+  assert launch.info()["split_k"] == 1            # 16 k-blocks: too short to split

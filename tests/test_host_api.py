@@ -40,14 +40,14 @@ def test_library_reports_missing_device_as_runtime_error_not_crash():
 
 
 def test_cfg_struct_layout_matches_header():
-  """The ctypes mirror of bg_cfg has the header's fields in order (sizes: 12 int32, int64, 2 int32)."""
+  """The ctypes mirror of bg_cfg has the header's fields in order (12 int32, int64, 5 int32, padded to 8 bytes)."""
   import ctypes
   from hopper_wgmma import _capi
   text = (ROOT / "include" / "sm100_gemm.h").read_text()
   body = text[text.index("typedef struct bg_cfg {"):text.index("} bg_cfg;")]
   fields = re.findall(r"int(?:32|64)_t\s+(\w+);", body)
   assert [f for f, _ in _capi.BgCfg._fields_] == fields
-  assert ctypes.sizeof(_capi.BgCfg) == 12 * 4 + 8 + 4 * 4
+  assert ctypes.sizeof(_capi.BgCfg) == 12 * 4 + 8 + 5 * 4 + 4
 
 
 # ----------------------------------------------------------------------------------------------------------------
@@ -96,6 +96,12 @@ def test_b200_knobs_validate():
     WSCfg(n_mma=2, acc_bufs=2)
   assert WSCfg(n_mma=2, cluster=2, tma_store=True).width == 512
   assert WSCfg().stages_used >= 2 and WSCfg(stages=3).stages_used == 3
+  with pytest.raises(ValueError, match="split_k must be"):
+    WSCfg(split_k=0)
+  with pytest.raises(ValueError, match="multiple of 32"):
+    WSCfg(BN=48, split_k=2)
+  assert WSCfg(split_k=4).name.endswith("_sk4") and WSCfg(split_k=4).to_c().split_k == 4
+  assert WSCfg(split_k=-1).name.endswith("_skA") and WSCfg(split_k=-1).to_c().split_k == -1
 
 
 # ----------------------------------------------------------------------------------------------------------------

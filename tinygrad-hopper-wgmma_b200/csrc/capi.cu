@@ -184,6 +184,10 @@ struct bg_plan {
   GemmParams kp{};
   int32_t* d_sched = nullptr;
   unsigned int* d_err = nullptr;
+  size_t partial_bytes = 0;          // split-K workspace, owned by the plan
+  size_t ticket_words = 0;
+  float* d_partial = nullptr;
+  unsigned int* d_tickets = nullptr;
   WsKernel ws = nullptr;
   RingKernel ring = nullptr;
   char name[96] = "";
@@ -264,6 +268,11 @@ int32_t take_error_word(int dev, unsigned int** out) {
 
 void free_plan(bg_plan* p) {
   if (p == nullptr) return;
+  if (p->d_partial || p->d_tickets) {
+    DeviceGuard guard(p->device);
+    if (p->d_partial) cudaFree(p->d_partial);
+    if (p->d_tickets) cudaFree(p->d_tickets);
+  }
   if (p->d_err) {
     DeviceStore& s = device_store(p->device);
     std::lock_guard<std::mutex> lock(s.mu);
@@ -366,6 +375,11 @@ int32_t setup_plan(const bg_cfg& c, int64_t M, int64_t N, int64_t K, const void*
   if (c.num_sm > 0 && c.num_sm < c.cluster) return fail(-1, "num_sm must be at least the cluster size");
   if (c.group_m < 1 || c.group_n < 1) return fail(-1, "group_m and group_n must be positive");
   if (c.acc_bufs < 0 || c.acc_bufs > 2) return fail(-1, "acc_bufs must be 0 (auto), 1 or 2");
+  // split_k: -1 = choose below, once the cluster count is known; 0 or 1 = off
+  if (c.split_k < -1 || c.split_k > 64) return fail(-1, "split_k must be -1 (auto) or in [0, 64]");
+  const bool sk_auto = c.split_k == -1;
+  int sk = c.split_k <= 1 ? 1 : c.split_k;
+  if (sk > 1 && c.kind != BG_KIND_WS) return fail(-1, "split_k needs the persistent kernel");
 
   const int bm = 64 * std::max(c.consumers, 1);
   const int cl = c.cluster;
@@ -393,8 +407,10 @@ int32_t setup_plan(const bg_cfg& c, int64_t M, int64_t N, int64_t K, const void*
   if (ragged) mt = (mt + cl - 1) / cl * cl;
   if (mt % cl) return fail(-1, "%lld row tiles not divisible by cluster %d", (long long)mt, cl);
   const int64_t cmt = mt / cl;
-  if (cmt > 0xFFFF || nt > 0xFFFF || cmt * nt > (1ll << 30) || nkb > (1ll << 30))
+  if (cmt > 0xFFFF || nt > 0xFFFF || cmt * nt * sk > (1ll << 30) || nkb * sk > (1ll << 30))
     return fail(-1, "problem too large for the tile table");
+  if (sk > 1 && sk > nkb) return fail(-1, "split_k %d exceeds the %lld k-blocks of K", sk, (long long)nkb);
+  if (sk > 1 && width % 32) return fail(-1, "split_k needs tiles a multiple of 32 columns wide (got %d)", width);
   if (A == nullptr || BT == nullptr || C == nullptr) return fail(-1, "null operand pointer");
   if ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(BT) | reinterpret_cast<uintptr_t>(C)) & 15)
     return fail(-1, "operand pointers must be 16-byte aligned");
@@ -512,7 +528,15 @@ int32_t setup_plan(const bg_cfg& c, int64_t M, int64_t N, int64_t K, const void*
   const int half = nblk == 2 ? bn : bn / 2;
   const bool narrow_ok = nblk == 2 || (half % 16 == 0 && (!c.tma_store || half % 64 == 0));
   int64_t n_entries = tiles;
-  if (c.kind == BG_KIND_WS && !c.no_tail_split && narrow_ok && !sched.empty()) {
+  // ---- automatic split-K: the most splits that still fit the tiles in one wave of clusters, each split keeping at
+  // least kAutoSplitMinKb k-blocks (below that the partial-sum round trip costs more than the split saves)
+  if (sk_auto && c.kind == BG_KIND_WS && width % 32 == 0) {
+    constexpr int kAutoSplitMinKb = 32, kAutoSplitMax = 16;
+    for (int s2 = 2; s2 <= kAutoSplitMax; ++s2)
+      if (tiles * s2 <= nclusters && nkb >= static_cast<int64_t>(kAutoSplitMinKb) * s2 && nkb * s2 <= (1ll << 30))
+        sk = s2;
+  }
+  if (c.kind == BG_KIND_WS && !c.no_tail_split && sk == 1 && narrow_ok && !sched.empty()) {
     const int64_t full = (tiles / nclusters) * nclusters;
     const int64_t tail = tiles - full;
     if (tail > 0 && 2 * tail <= nclusters) {
@@ -530,6 +554,18 @@ int32_t setup_plan(const bg_cfg& c, int64_t M, int64_t N, int64_t K, const void*
     }
   }
   if (nt * 2 > 0x7FFF) return fail(-1, "too many column tiles (%lld) for the tile table", (long long)nt);
+  // ---- split-K: every tile becomes sk consecutive entries (split s = entry % sk), dealt to consecutive clusters
+  if (sk > 1) {
+    std::vector<int32_t> ext;
+    ext.reserve(sched.size() * sk);
+    for (int32_t e : sched)
+      for (int s = 0; s < sk; ++s) ext.push_back(e);
+    sched.swap(ext);
+    n_entries = static_cast<int64_t>(sched.size());
+    sched_key[1] |= sk << 1;
+    p->partial_bytes = static_cast<size_t>(n_entries) * cl * 4u * 32u * static_cast<size_t>(width) * sizeof(float);
+    p->ticket_words = static_cast<size_t>(tiles) * cl * 4u;
+  }
   nclusters = std::min<int64_t>(nclusters, n_entries);
   p->grid = static_cast<int>(nclusters * (c.kind == BG_KIND_RING ? 1 : cl));
 
@@ -575,15 +611,19 @@ int32_t setup_plan(const bg_cfg& c, int64_t M, int64_t N, int64_t K, const void*
   kp.err = nullptr;
   kp.budget_ns = c.wait_budget_ns > 0 ? static_cast<unsigned long long>(c.wait_budget_ns) : 4000000000ull;
   kp.skip_job = c.debug_skip_job;
+  kp.split_k = sk;
+  kp.partial = nullptr;
+  kp.tickets = nullptr;
   // split accumulator (two N blocks, one 512-column buffer): how many k-blocks run on half 0 alone at a tile's start
   // and end; it must stay below the ring depth so the producer keeps a free stage
   kp.look = std::max(1, std::min(2, stages - 2));
   // the first wave of the tile table also travels in the kernel parameters (see FirstTile in the kernel)
   for (size_t i = 0; i < sched.size() && i < static_cast<size_t>(sm100::kFirstWave); ++i) kp.first_wave[i] = sched[i];
 
-  snprintf(p->name, sizeof(p->name), "%s<BM=%d,%s,%s> BN=%dx%d stages=%d acc=%d tail=%d", c.kind == BG_KIND_RING ? "sm100_gemm_ring" : "sm100_gemm_ws",
-           bm, paired ? "pair" : (cl == 2 ? "cluster2" : "cta"), p->tma_store ? "tma_store" : "reg_store", bn, nblk,
-           stages, acc_bufs, p->narrow_tiles);
+  snprintf(p->name, sizeof(p->name), "%s<BM=%d,%s,%s> BN=%dx%d stages=%d acc=%d tail=%d splitk=%d",
+           c.kind == BG_KIND_RING ? "sm100_gemm_ring" : "sm100_gemm_ws", bm,
+           paired ? "pair" : (cl == 2 ? "cluster2" : "cta"), p->tma_store ? "tma_store" : "reg_store", bn, nblk,
+           stages, acc_bufs, p->narrow_tiles, sk);
   return 0;
 }
 
@@ -607,8 +647,19 @@ int32_t bg_plan_create(bg_plan** out, const bg_cfg* cfg, int64_t M, int64_t N, i
   // ---- device buffers: tile table (cached per schedule) and error word (from the device's slab)
   if (!sched.empty() && (st = store_table(device, sched_key, sched, &p->d_sched))) return st;
   if ((st = take_error_word(device, &p->d_err))) return st;
+  if (p->partial_bytes > 0) {
+    // split-K workspace: partial sums (fully written before they are read) and zeroed arrival words
+    cudaError_t e = cudaMalloc(&p->d_partial, p->partial_bytes);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(split-K partial sums)");
+    if ((e = cudaMalloc(&p->d_tickets, p->ticket_words * sizeof(unsigned int))) != cudaSuccess)
+      return cuda_fail(e, "cudaMalloc(split-K arrival words)");
+    if ((e = cudaMemset(p->d_tickets, 0, p->ticket_words * sizeof(unsigned int))) != cudaSuccess)
+      return cuda_fail(e, "cudaMemset(split-K arrival words)");
+  }
   p->kp.sched = p->d_sched;
   p->kp.err = p->d_err;
+  p->kp.partial = p->d_partial;
+  p->kp.tickets = p->d_tickets;
   *out = p.release();
   return 0;
 }
@@ -650,6 +701,8 @@ int32_t bg_gemm_noalloc(const bg_cfg* cfg, int64_t M, int64_t N, int64_t K, cons
                         uint32_t* err_word) {
   if (cfg == nullptr) return fail(-1, "null cfg pointer");
   if (device < 0 || device >= 64) return fail(-1, "device %d out of range", device);
+  if (cfg->split_k > 1)
+    return fail(-1, "bg_gemm_noalloc has no split-K workspace (split_k = %d); use bg_plan_create", cfg->split_k);
   bg_plan plan;   // lives on this stack frame and owns no device memory
   std::vector<int32_t> sched;
   std::array<int, 8> sched_key{};
@@ -730,6 +783,8 @@ int32_t bg_plan_check_error(bg_plan* p, void* stream, uint32_t* err_word) {
   if (err_word) *err_word = w;
   if (w != 0) {
     cudaMemset(p->d_err, 0, sizeof(uint32_t));
+    // an interrupted split-K launch can leave arrival words behind; the next launch needs them zero
+    if (p->d_tickets) cudaMemset(p->d_tickets, 0, p->ticket_words * sizeof(unsigned int));
     static const char* roles[] = {"?", "producer (free stage)", "MMA (loaded stage)", "MMA (free accumulator)",
                                   "epilogue (finished accumulator)", "MMA drain", "load drain"};
     const uint32_t role = w >> 24;
@@ -755,6 +810,7 @@ int32_t bg_plan_get_info(const bg_plan* p, bg_plan_info* info) {
   info->tmem_cols = static_cast<int32_t>(p->kp.tmem_cols);
   info->max_active_clusters = p->max_active_clusters;
   info->narrow_tiles = p->narrow_tiles;
+  info->split_k = p->kp.split_k;
   snprintf(info->kernel, sizeof(info->kernel), "%s", p->name);
   return 0;
 }

@@ -79,8 +79,25 @@ struct GemmParams {
   unsigned long long budget_ns;  // per-wait time limit
   int look;                // split accumulator: k-blocks of the half-0-first phases at tile start and end (< stages)
   int skip_job;            // test hook: the producer never loads this job index (-1 = off); makes waits run out
+  int split_k;             // K splits per output tile (1 = off): entry i computes split i % split_k of tile
+                           // i / split_k, k-blocks [s * num_kb / split_k, (s + 1) * num_kb / split_k)
+  float* partial;          // split-K: fp32 partial sums, one 32-lane x width slice per (entry, CTA of the pair, warp)
+  unsigned int* tickets;   // split-K: one arrival word per (tile, CTA of the pair, warp), counting entries whose
+                           // partial sums are written; zero between launches
   int32_t first_wave[kFirstWave];  // sched[0 .. min(tiles, kFirstWave)) again, delivered with the launch
 };
+
+// K range of schedule entry idx: k-blocks [kb0, kb0 + nk).
+__device__ __forceinline__ void k_range(const GemmParams& p, int idx, int& kb0, int& nk) {
+  if (p.split_k > 1) {
+    const int s = idx % p.split_k;
+    kb0 = s * p.num_kb / p.split_k;
+    nk = (s + 1) * p.num_kb / p.split_k - kb0;
+  } else {
+    kb0 = 0;
+    nk = p.num_kb;
+  }
+}
 
 __device__ __forceinline__ void record_error(unsigned int* err, uint32_t role, uint32_t counter) {
   atomicCAS(err, 0u, role | (counter > 0xFFFFFFu ? 0xFFFFFFu : counter));
@@ -253,7 +270,9 @@ __global__ void __launch_bounds__(kWsThreads, 1)
       const uint32_t tx = narrow ? p.tx_narrow : p.tx_bytes;
       const int row_a = (cm * p.cl + static_cast<int>(rank)) * BM;
       const int row_b = tn * width + (PAIRED ? static_cast<int>(rank) * (bsub / 2) : 0);
-      for (int kb = 0; kb < p.num_kb; ++kb, ++job) {
+      int kb0, nk;
+      k_range(p, idx, kb0, nk);
+      for (int kb = kb0; kb < kb0 + nk; ++kb, ++job) {
         if (!mbar_wait_warp(empty0 + 8u * stage, phase ^ 1u, budget)) {
           if (lane == 0) record_error(p.err, kErrProducer, job);
           failed = true;
@@ -362,7 +381,8 @@ __global__ void __launch_bounds__(kWsThreads, 1)
         first.coords(p, idx, cm, tn, narrow);
         const int nblk = (narrow && NB == 2) ? 1 : NB;
         const uint32_t idesc = (narrow && NB == 1) ? p.idesc_narrow : p.idesc;
-        const int nk = p.num_kb;
+        int kb0, nk;   // the MMAs count k-blocks from 0 within the entry's K range: the first one overwrites D
+        k_range(p, idx, kb0, nk);
         if (!split) {
           if (!wait_acc(tempty0 + 8u * acc, acc_phase ^ 1u, i)) break;
           const uint32_t d = tmem_base + acc * static_cast<uint32_t>(p.acc_stride);
@@ -479,6 +499,103 @@ __global__ void __launch_bounds__(kWsThreads, 1)
     const uint32_t my_stage = sC + static_cast<uint32_t>(q) * 2u * STAGE_C;
     const bool split = NB == 2 && p.acc_bufs == 1;
     uint32_t acc = 0, acc_phase = 0, chunk = 0;
+    // Split-K (p.split_k > 1). The split_k entries of a tile run on different clusters, each into its own
+    // accumulator. Per (tile, CTA, warp) an arrival word counts finished entries: every entry writes its fp32 partial
+    // sums to its own workspace slice, makes them visible at gpu scope and then counts itself. The entry that sees
+    // the count reach split_k - 1 is the last: every other entry's partial sums are visible to it. It adds all
+    // splits in split order (its own from tensor memory), so the rounding does not depend on which entry came last,
+    // stores C and resets the word for the next launch. No entry waits for another.
+    const size_t sk_slice = 32u * static_cast<size_t>(p.bn * NB);                 // floats per slice
+    const size_t sk_stride = static_cast<size_t>(p.cl) * 4u * sk_slice;           // between consecutive splits
+    int sk_own = 0;                  // this entry's split
+    unsigned int* sk_word = nullptr;   // the tile's arrival word for this warp
+    float* sk_src = nullptr;         // this warp's slice of split 0 of the tile
+    // Entry idx's split, arrival word and workspace slices.
+    auto sk_setup = [&](int idx) {
+      const int tile = idx / p.split_k;
+      sk_own = idx - tile * p.split_k;
+      sk_word = p.tickets + (static_cast<size_t>(tile) * p.cl + rank) * 4u + static_cast<size_t>(q);
+      sk_src = p.partial + ((static_cast<size_t>(tile) * p.split_k * p.cl + rank) * 4u + q) * sk_slice;
+    };
+    // Count this entry once all its partial sums are written; true for the last entry of the tile.
+    auto sk_count = [&]() {
+      __threadfence();   // this lane's partial sums are visible at gpu scope before the count
+      __syncwarp();
+      uint32_t prev = 0;
+      if (lane == 0) {
+        prev = atomicAdd(sk_word, 1u);
+        __threadfence();   // acquire: the partial sums counted before this entry are visible from here on
+      }
+      prev = __shfl_sync(0xffffffffu, prev, 0);
+      __syncwarp();
+      const bool last = static_cast<int>(prev) == p.split_k - 1;
+      if (last && lane == 0) atomicExch(sk_word, 0u);   // every split has counted: free for the next launch
+      return last;
+    };
+    // Last entry: replace accumulator columns [0, ncols) at TMEM address tacc (tile-relative columns
+    // [tcol, tcol + ncols)) by the sum over all splits, in place in tensor memory, 32 columns at a time. The other
+    // splits' slices are read in units of 32 columns of one split, two units in flight. Slice layout: float4 g of
+    // lane l at (g * 32 + l) * 4, g = column / 4.
+    auto sk_reduce = [&](uint32_t tacc, int tcol, int ncols) {
+      const int others = p.split_k - 1;
+      const int units = (ncols >> 5) * others;   // unit u: chunk u / others of the (u % others)-th other split
+      auto load = [&](int u, uint32_t (&x)[32]) {
+        const int c = u / others, j = u - c * others;
+        const int s = j < sk_own ? j : j + 1;
+        const float* src = sk_src + static_cast<size_t>(s) * sk_stride +
+                           (static_cast<size_t>((tcol >> 2) + 8 * c) * 32u + static_cast<size_t>(lane)) * 4u;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) ld_global_cg_v4(src + i * 128, x[4 * i], x[4 * i + 1], x[4 * i + 2], x[4 * i + 3]);
+      };
+      float a[32];
+      auto add_own = [&](int c, bool first) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(tacc + 32u * c, v);
+        tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 32; ++j) a[j] = first ? __uint_as_float(v[j]) : a[j] + __uint_as_float(v[j]);
+      };
+      // fold unit u (split s of chunk c) into the running sum in the order 0, 1, ..., split_k - 1
+      auto consume = [&](int u, const uint32_t (&x)[32]) {
+        const int c = u / others, j = u - c * others;
+        const int s = j < sk_own ? j : j + 1;
+        if (j == 0 && sk_own == 0) add_own(c, true);
+        else if (j > 0 && sk_own == s - 1) add_own(c, false);
+        const bool first = j == 0 && sk_own != 0;   // split 0 starts the sum
+#pragma unroll
+        for (int e = 0; e < 32; ++e) a[e] = first ? __uint_as_float(x[e]) : a[e] + __uint_as_float(x[e]);
+        if (j == others - 1) {
+          if (sk_own == p.split_k - 1) add_own(c, false);
+          uint32_t v[32];
+#pragma unroll
+          for (int e = 0; e < 32; ++e) v[e] = __float_as_uint(a[e]);
+          tmem_st_32x32b_x32(tacc + 32u * c, v);
+        }
+      };
+      uint32_t xa[32], xb[32];
+      load(0, xa);
+#pragma unroll 1
+      for (int u = 0; u < units; u += 2) {
+        if (u + 1 < units) load(u + 1, xb);
+        consume(u, xa);
+        if (u + 2 < units) load(u + 2, xa);
+        if (u + 1 < units) consume(u + 1, xb);
+      }
+      tmem_st_wait();
+    };
+    // Write accumulator columns [0, ncols) at TMEM address tacc (tile-relative columns [tcol, tcol + ncols)) as fp32
+    // into the slice `dst`.
+    auto put_partial = [&](uint32_t tacc, int tcol, int ncols, float* dst) {
+      float* d = dst + (static_cast<size_t>(tcol >> 2) * 32u + static_cast<size_t>(lane)) * 4u;
+#pragma unroll 1
+      for (int c = 0; c < (ncols >> 5); ++c) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(tacc + 32u * c, v);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 8; ++i) st_global_v4(d + (8 * c + i) * 128, v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+      }
+    };
     // Write accumulator columns starting at TMEM address tacc (this warp's lanes) to C rows row0.., columns
     // [ccol, ccol + ncols).
     auto drain = [&](uint32_t tacc, int row0, int ccol, int ncols) {
@@ -540,7 +657,8 @@ __global__ void __launch_bounds__(kWsThreads, 1)
       const int width = narrow ? p.bn * NB / 2 : p.bn * NB;   // output columns of this tile
       const int col0 = tn * width;
       if (split) {
-        // half h = TMEM columns [h * bn, (h + 1) * bn) with its own barriers; a half-width tile has only half 0
+        // half h = TMEM columns [h * bn, (h + 1) * bn) with its own barriers; a half-width tile has only half 0.
+        // Under split-K both halves are held until the entry has counted itself.
         bool ok = true;
         for (int h = 0; h < 2; ++h) {
           if (!mbar_wait_warp(tfull0 + 8u * h, acc_phase, budget)) {
@@ -549,11 +667,27 @@ __global__ void __launch_bounds__(kWsThreads, 1)
             break;
           }
           tc_fence_after();
-          if (h == 0 || !narrow)
-            drain(tmem_base + lane_base + static_cast<uint32_t>(h * p.bn), row0, col0 + h * p.bn, p.bn);
+          const uint32_t tacc = tmem_base + lane_base + static_cast<uint32_t>(h * p.bn);
+          if (p.split_k > 1) {
+            if (h == 0) sk_setup(idx);
+            put_partial(tacc, h * p.bn, p.bn, sk_src + static_cast<size_t>(sk_own) * sk_stride);
+            continue;
+          }
+          if (h == 0 || !narrow) drain(tacc, row0, col0 + h * p.bn, p.bn);
           release(tempty0 + 8u * h);
         }
         if (!ok) break;
+        if (p.split_k > 1) {
+          const bool last = sk_count();
+          for (int h = 0; h < 2; ++h) {
+            const uint32_t tacc = tmem_base + lane_base + static_cast<uint32_t>(h * p.bn);
+            if (last) {
+              sk_reduce(tacc, h * p.bn, p.bn);
+              drain(tacc, row0, col0 + h * p.bn, p.bn);
+            }
+            release(tempty0 + 8u * h);
+          }
+        }
         acc_phase ^= 1u;
         continue;
       }
@@ -562,7 +696,17 @@ __global__ void __launch_bounds__(kWsThreads, 1)
         break;
       }
       tc_fence_after();
-      drain(tmem_base + lane_base + acc * static_cast<uint32_t>(p.acc_stride), row0, col0, width);
+      const uint32_t tacc = tmem_base + lane_base + acc * static_cast<uint32_t>(p.acc_stride);
+      if (p.split_k > 1) {
+        sk_setup(idx);
+        put_partial(tacc, 0, width, sk_src + static_cast<size_t>(sk_own) * sk_stride);
+        if (sk_count()) {
+          sk_reduce(tacc, 0, width);
+          drain(tacc, row0, col0, width);
+        }
+      } else {
+        drain(tacc, row0, col0, width);
+      }
       release(tempty0 + 8u * acc);
       if (++acc == static_cast<uint32_t>(p.acc_bufs)) {
         acc = 0;

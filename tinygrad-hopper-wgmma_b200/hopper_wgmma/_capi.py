@@ -25,7 +25,7 @@ class BgCfg(ctypes.Structure):
               ("group_n", ctypes.c_int32), ("tma_store", ctypes.c_int32), ("cluster", ctypes.c_int32),
               ("hilbert", ctypes.c_int32), ("acc_bufs", ctypes.c_int32), ("wait_budget_ns", ctypes.c_int64),
               ("debug_skip_job", ctypes.c_int32), ("n_mma", ctypes.c_int32),
-              ("no_tail_split", ctypes.c_int32), ("ragged", ctypes.c_int32)]
+              ("no_tail_split", ctypes.c_int32), ("ragged", ctypes.c_int32), ("split_k", ctypes.c_int32)]
 
 
 class BgPlanInfo(ctypes.Structure):
@@ -33,7 +33,7 @@ class BgPlanInfo(ctypes.Structure):
               ("stages", ctypes.c_int32), ("tiles", ctypes.c_int32), ("clusters", ctypes.c_int32),
               ("cluster", ctypes.c_int32), ("paired", ctypes.c_int32), ("bm", ctypes.c_int32), ("bn", ctypes.c_int32),
               ("acc_bufs", ctypes.c_int32), ("tmem_cols", ctypes.c_int32), ("max_active_clusters", ctypes.c_int32),
-              ("narrow_tiles", ctypes.c_int32), ("kernel", ctypes.c_char * 96)]
+              ("narrow_tiles", ctypes.c_int32), ("split_k", ctypes.c_int32), ("kernel", ctypes.c_char * 96)]
 
 
 def _load() -> ctypes.CDLL:
@@ -102,7 +102,7 @@ def grouped_order(m_tiles: int, n_tiles: int, group_m: int, group_n: int) -> lis
 
 
 class Plan:
-  """Owns one ``bg_plan``: encoded tensor maps, the device tile table and the error word."""
+  """Owns one ``bg_plan``: encoded tensor maps, the device tile table, the error word and any split-K workspace."""
 
   def __init__(self, cfg: BgCfg, M: int, N: int, K: int, a_ptr: int, lda: int, bt_ptr: int, ldb: int, c_ptr: int,
                ldc: int, device: int):

@@ -144,6 +144,8 @@ class WSCfg:
   n_mma: int = 1               # tcgen05.mma instructions along N per K step: tiles are n_mma * BN columns wide
   split_tail: bool = True      # split a last wave that is at most half full into half-width tiles
   ragged: bool = False         # accept any M (and N, K multiples of 8): edge tiles are zero-filled / clipped
+  split_k: int = 1             # K splits per output tile (fp32 partial sums reduced in-kernel by the last split);
+                               # -1 = chosen per shape (only shapes with few tiles and long K are split)
 
   def __post_init__(self):
     if self.BK != 64: raise ValueError("BK must be 64 (one 128-byte swizzle atom)")
@@ -157,6 +159,8 @@ class WSCfg:
     if self.regs is not None and (len(self.regs) != 2 or any(r % 8 or not 24 <= r <= 256 for r in self.regs)):
       raise ValueError("regs must be two multiples of 8 in [24, 256]")
     if self.n_mma not in (1, 2): raise ValueError("n_mma must be 1 or 2")
+    if self.split_k != -1 and not 1 <= self.split_k <= 64: raise ValueError("split_k must be -1 (auto) or in [1, 64]")
+    if self.split_k > 1 and self.width % 32: raise ValueError("split_k needs tiles a multiple of 32 columns wide")
     if self.acc_bufs is not None and self.acc_bufs not in (1, 2): raise ValueError("acc_bufs must be 1 or 2")
     if self.acc_bufs == 2 and 2 * self.width > 512: raise ValueError("two accumulators of the tile width exceed tensor memory")
     if self.stages_used < 2: raise ValueError(f"not even 2 stages fit in {SMEM_LIMIT} bytes of shared memory")
@@ -195,7 +199,7 @@ class WSCfg:
     return (f"ws_c{self.consumers}_s{st}_n{self.BN}_sm{sm}_g{self.group_m}x{self.group_n}"
             f"{'_tmast' if self.tma_store else ''}{'_hil' if self.hilbert else ''}"
             f"{f'_r{self.regs[0]}x{self.regs[1]}' if self.regs else ''}{f'_cl{self.cluster}' if self.cluster > 1 else ''}"
-            f"{f'_x{self.n_mma}' if self.n_mma > 1 else ''}")
+            f"{f'_x{self.n_mma}' if self.n_mma > 1 else ''}{f'_sk{self.split_k}' if self.split_k > 1 else '_skA' if self.split_k == -1 else ''}")
 
   def to_c(self, kind: int = _capi.KIND_WS, num_sm: int | None = None, wait_budget_ns: int = 0,
            debug_skip_job: int = -1) -> _capi.BgCfg:
@@ -203,7 +207,8 @@ class WSCfg:
                        num_sm=num_sm or self.num_sm or 0, group_m=self.group_m, group_n=self.group_n,
                        tma_store=int(self.tma_store), cluster=self.cluster, hilbert=int(self.hilbert),
                        acc_bufs=self.acc_bufs or 0, wait_budget_ns=wait_budget_ns, debug_skip_job=debug_skip_job,
-                       n_mma=self.n_mma, no_tail_split=0 if self.split_tail else 1, ragged=int(self.ragged))
+                       n_mma=self.n_mma, no_tail_split=0 if self.split_tail else 1, ragged=int(self.ragged),
+                       split_k=self.split_k)
 
 
 # =============================================================================================================

@@ -60,3 +60,16 @@ EXTRA = {
   "tma_store_132": WSCfg(tma_store=True, num_sm=132),
   "tma_store_128": WSCfg(tma_store=True, num_sm=128),
 }
+
+
+def lookup(name: str):
+  """A config by name from LADDER, SWEEP, B200 or EXTRA. ``<name>@sk<S>`` is that config with ``split_k=S``
+  (e.g. ``cta_n128@sk2``; ``@skA`` = automatic), so that sweeps can try K splits on any tile shape."""
+  import dataclasses
+  base, _, mod = name.partition("@")
+  cfg = {**LADDER, **SWEEP, **EXTRA, **B200}[base]
+  if not mod: return cfg
+  if not mod.startswith("sk") or not (mod[2:].isdigit() or mod[2:] == "A"):
+    raise KeyError(f"unknown config modifier {mod!r} in {name!r}")
+  if not isinstance(cfg, WSCfg): raise ValueError(f"{base} is not a persistent config: no split_k")
+  return dataclasses.replace(cfg, split_k=-1 if mod[2:] == "A" else int(mod[2:]))

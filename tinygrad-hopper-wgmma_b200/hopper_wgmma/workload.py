@@ -4,9 +4,11 @@
     python -m hopper_wgmma.workload --shape 4096 --configs tma_store,hilbert --reps 5 --torch --check [--time]
 
   --shape MxNxK   problem size (or a single N for a square GEMM)
-  --configs a,b   names from ladder.LADDER / SWEEP / EXTRA (or "all"); configs invalid for the shape print SKIP
+  --configs a,b   names from ladder.LADDER / SWEEP / EXTRA / B200 (or "all"), optionally with a split-K suffix
+                  (``cta_n128@sk2``); configs invalid for the shape print SKIP
   --torch         also launch cuBLAS (torch.matmul) on the same inputs
-  --check         compare each config with cuBLAS once, on NaN-poisoned output, before the timed launches
+  --check         compare each config once, on NaN-poisoned output, with the fp32 product of the same bf16 inputs
+                  (cuBLAS in fp32, TF32 off) before the timed launches
   --time          time each config with CUDA events (best and mean of --reps launches, after warm-up) and print
                   one JSON line per config; without it the script only launches, for Nsight Compute to time
   --flush         with --time: rewrite a 256 MiB buffer between launches so every launch starts with a cold L2
@@ -69,7 +71,7 @@ def _time(fn, reps: int, warmup: int, flush=None) -> tuple[float, float]:
 def main(argv=None) -> int:
   import torch
 
-  from .ladder import B200, EXTRA, LADDER, SWEEP, build
+  from .ladder import B200, EXTRA, LADDER, SWEEP, build, lookup
   ap = argparse.ArgumentParser()
   ap.add_argument("--shape", default="4096")
   ap.add_argument("--configs", default="")
@@ -90,7 +92,12 @@ def main(argv=None) -> int:
   c = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
   flush = torch.empty(64 << 20, dtype=torch.int32, device=dev) if args.flush else None   # 256 MiB
   flops = 2.0 * M * N * K
-  ref = (a @ b).float() if (args.check or args.torch) else None
+  ref = None
+  if args.check:   # fp32 product of the bf16 inputs (no TF32): the oracle's arithmetic, on the GPU
+    tf32 = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    ref = a.float() @ b.float()
+    torch.backends.cuda.matmul.allow_tf32 = tf32
   cub_us = None
   if args.torch:
     out = torch.empty_like(c)
@@ -104,8 +111,8 @@ def main(argv=None) -> int:
                                   "us_mean": round(mean, 2), "tflops": round(flops / best / 1e6, 1)}), flush=True)
   failed = 0
   for name in names:
-    cfg = table[name]
     try:
+      cfg = lookup(name)
       run = build(N, cfg, M, K)
       launch = run(a, b, c)
       c.fill_(float("nan"))          # a skipped write can't pass the check
