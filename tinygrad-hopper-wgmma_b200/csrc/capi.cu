@@ -137,18 +137,20 @@ using WsKernel = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMa
                           const GemmParams);
 using RingKernel = void (*)(const CUtensorMap, const CUtensorMap, const GemmParams);
 
-template <int NB>
+// Split-K is a template switch so that the kernels without it carry none of its code or registers.
+template <int NB, bool SK>
 WsKernel pick_ws_nb(int bm, bool paired, bool tma_store) {
   using namespace sm100;
   if (bm == 128) {
-    if (paired) return tma_store ? sm100_gemm_ws<128, true, true, NB> : sm100_gemm_ws<128, true, false, NB>;
-    return tma_store ? sm100_gemm_ws<128, false, true, NB> : sm100_gemm_ws<128, false, false, NB>;
+    if (paired) return tma_store ? sm100_gemm_ws<128, true, true, NB, SK> : sm100_gemm_ws<128, true, false, NB, SK>;
+    return tma_store ? sm100_gemm_ws<128, false, true, NB, SK> : sm100_gemm_ws<128, false, false, NB, SK>;
   }
-  return tma_store ? sm100_gemm_ws<64, false, true, NB> : sm100_gemm_ws<64, false, false, NB>;
+  return tma_store ? sm100_gemm_ws<64, false, true, NB, SK> : sm100_gemm_ws<64, false, false, NB, SK>;
 }
 
-WsKernel pick_ws(int bm, bool paired, bool tma_store, int nblk) {
-  return nblk == 2 ? pick_ws_nb<2>(bm, paired, tma_store) : pick_ws_nb<1>(bm, paired, tma_store);
+WsKernel pick_ws(int bm, bool paired, bool tma_store, int nblk, bool split_k) {
+  if (split_k) return nblk == 2 ? pick_ws_nb<2, true>(bm, paired, tma_store) : pick_ws_nb<1, true>(bm, paired, tma_store);
+  return nblk == 2 ? pick_ws_nb<2, false>(bm, paired, tma_store) : pick_ws_nb<1, false>(bm, paired, tma_store);
 }
 
 RingKernel pick_ring(int bm) { return bm == 128 ? sm100::sm100_gemm_ring<128> : sm100::sm100_gemm_ring<64>; }
@@ -474,13 +476,23 @@ int32_t setup_plan(const bg_cfg& c, int64_t M, int64_t N, int64_t K, const void*
     }
   }
 
+  // ---- automatic split-K: the most splits that still fit the tiles in one wave of clusters
+  // (num_sm / cluster of them), each split keeping at least kAutoSplitMinKb k-blocks (below that the partial-sum
+  // round trip costs more than the split saves)
+  if (sk_auto && c.kind == BG_KIND_WS && width % 32 == 0) {
+    constexpr int kAutoSplitMinKb = 32, kAutoSplitMax = 16;
+    for (int s2 = 2; s2 <= kAutoSplitMax; ++s2)
+      if (tiles * s2 <= nclusters && nkb >= static_cast<int64_t>(kAutoSplitMinKb) * s2 && nkb * s2 <= (1ll << 30))
+        sk = s2;
+  }
+
   // ---- kernel and launch attributes
   const void* fn = nullptr;
   if (c.kind == BG_KIND_RING) {
     p->ring = pick_ring(bm);
     fn = reinterpret_cast<const void*>(p->ring);
   } else {
-    p->ws = pick_ws(bm, paired, p->tma_store, nblk);
+    p->ws = pick_ws(bm, paired, p->tma_store, nblk, sk > 1);
     fn = reinterpret_cast<const void*>(p->ws);
   }
   cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_optin);
@@ -528,14 +540,6 @@ int32_t setup_plan(const bg_cfg& c, int64_t M, int64_t N, int64_t K, const void*
   const int half = nblk == 2 ? bn : bn / 2;
   const bool narrow_ok = nblk == 2 || (half % 16 == 0 && (!c.tma_store || half % 64 == 0));
   int64_t n_entries = tiles;
-  // ---- automatic split-K: the most splits that still fit the tiles in one wave of clusters, each split keeping at
-  // least kAutoSplitMinKb k-blocks (below that the partial-sum round trip costs more than the split saves)
-  if (sk_auto && c.kind == BG_KIND_WS && width % 32 == 0) {
-    constexpr int kAutoSplitMinKb = 32, kAutoSplitMax = 16;
-    for (int s2 = 2; s2 <= kAutoSplitMax; ++s2)
-      if (tiles * s2 <= nclusters && nkb >= static_cast<int64_t>(kAutoSplitMinKb) * s2 && nkb * s2 <= (1ll << 30))
-        sk = s2;
-  }
   if (c.kind == BG_KIND_WS && !c.no_tail_split && sk == 1 && narrow_ok && !sched.empty()) {
     const int64_t full = (tiles / nclusters) * nclusters;
     const int64_t tail = tiles - full;

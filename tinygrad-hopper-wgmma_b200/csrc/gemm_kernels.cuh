@@ -87,9 +87,11 @@ struct GemmParams {
   int32_t first_wave[kFirstWave];  // sched[0 .. min(tiles, kFirstWave)) again, delivered with the launch
 };
 
-// K range of schedule entry idx: k-blocks [kb0, kb0 + nk).
+// K range of schedule entry idx: k-blocks [kb0, kb0 + nk). Kernels built without split-K (SPLITK = false) ignore
+// p.split_k; the host never hands them a split schedule.
+template <bool SPLITK>
 __device__ __forceinline__ void k_range(const GemmParams& p, int idx, int& kb0, int& nk) {
-  if (p.split_k > 1) {
+  if (SPLITK && p.split_k > 1) {
     const int s = idx % p.split_k;
     kb0 = s * p.num_kb / p.split_k;
     nk = (s + 1) * p.num_kb / p.split_k - kb0;
@@ -188,7 +190,7 @@ __device__ __forceinline__ void epilogue_registers(uint32_t tacc, __nv_bfloat16*
   }
 }
 
-template <int BM, bool PAIRED, bool TMA_STORE, int NB>
+template <int BM, bool PAIRED, bool TMA_STORE, int NB, bool SPLITK>
 __global__ void __launch_bounds__(kWsThreads, 1)
     sm100_gemm_ws(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                   const __grid_constant__ CUtensorMap tmBn, const __grid_constant__ CUtensorMap tmC,
@@ -271,7 +273,7 @@ __global__ void __launch_bounds__(kWsThreads, 1)
       const int row_a = (cm * p.cl + static_cast<int>(rank)) * BM;
       const int row_b = tn * width + (PAIRED ? static_cast<int>(rank) * (bsub / 2) : 0);
       int kb0, nk;
-      k_range(p, idx, kb0, nk);
+      k_range<SPLITK>(p, idx, kb0, nk);
       for (int kb = kb0; kb < kb0 + nk; ++kb, ++job) {
         if (!mbar_wait_warp(empty0 + 8u * stage, phase ^ 1u, budget)) {
           if (lane == 0) record_error(p.err, kErrProducer, job);
@@ -382,7 +384,7 @@ __global__ void __launch_bounds__(kWsThreads, 1)
         const int nblk = (narrow && NB == 2) ? 1 : NB;
         const uint32_t idesc = (narrow && NB == 1) ? p.idesc_narrow : p.idesc;
         int kb0, nk;   // the MMAs count k-blocks from 0 within the entry's K range: the first one overwrites D
-        k_range(p, idx, kb0, nk);
+        k_range<SPLITK>(p, idx, kb0, nk);
         if (!split) {
           if (!wait_acc(tempty0 + 8u * acc, acc_phase ^ 1u, i)) break;
           const uint32_t d = tmem_base + acc * static_cast<uint32_t>(p.acc_stride);
@@ -668,7 +670,7 @@ __global__ void __launch_bounds__(kWsThreads, 1)
           }
           tc_fence_after();
           const uint32_t tacc = tmem_base + lane_base + static_cast<uint32_t>(h * p.bn);
-          if (p.split_k > 1) {
+          if (SPLITK && p.split_k > 1) {
             if (h == 0) sk_setup(idx);
             put_partial(tacc, h * p.bn, p.bn, sk_src + static_cast<size_t>(sk_own) * sk_stride);
             continue;
@@ -677,7 +679,7 @@ __global__ void __launch_bounds__(kWsThreads, 1)
           release(tempty0 + 8u * h);
         }
         if (!ok) break;
-        if (p.split_k > 1) {
+        if (SPLITK && p.split_k > 1) {
           const bool last = sk_count();
           for (int h = 0; h < 2; ++h) {
             const uint32_t tacc = tmem_base + lane_base + static_cast<uint32_t>(h * p.bn);
@@ -697,7 +699,7 @@ __global__ void __launch_bounds__(kWsThreads, 1)
       }
       tc_fence_after();
       const uint32_t tacc = tmem_base + lane_base + acc * static_cast<uint32_t>(p.acc_stride);
-      if (p.split_k > 1) {
+      if (SPLITK && p.split_k > 1) {
         sk_setup(idx);
         put_partial(tacc, 0, width, sk_src + static_cast<size_t>(sk_own) * sk_stride);
         if (sk_count()) {

@@ -63,13 +63,18 @@ EXTRA = {
 
 
 def lookup(name: str):
-  """A config by name from LADDER, SWEEP, B200 or EXTRA. ``<name>@sk<S>`` is that config with ``split_k=S``
-  (e.g. ``cta_n128@sk2``; ``@skA`` = automatic), so that sweeps can try K splits on any tile shape."""
+  """A config by name from LADDER, SWEEP, B200 or EXTRA, with optional ``@`` modifiers so that sweeps can vary one
+  knob on any tile shape: ``@sk<S>`` sets ``split_k=S`` (``@skA`` = automatic), ``@reg`` selects the register
+  epilogue (``tma_store=False``). Example: ``cta_n128@sk2``, ``cta_n64@reg@skA``."""
   import dataclasses
-  base, _, mod = name.partition("@")
+  base, *mods = name.split("@")
   cfg = {**LADDER, **SWEEP, **EXTRA, **B200}[base]
-  if not mod: return cfg
-  if not mod.startswith("sk") or not (mod[2:].isdigit() or mod[2:] == "A"):
-    raise KeyError(f"unknown config modifier {mod!r} in {name!r}")
-  if not isinstance(cfg, WSCfg): raise ValueError(f"{base} is not a persistent config: no split_k")
-  return dataclasses.replace(cfg, split_k=-1 if mod[2:] == "A" else int(mod[2:]))
+  for mod in mods:
+    if not isinstance(cfg, WSCfg): raise ValueError(f"{base} is not a persistent config: no @{mod}")
+    if mod == "reg":
+      cfg = dataclasses.replace(cfg, tma_store=False)
+    elif mod.startswith("sk") and (mod[2:].isdigit() or mod[2:] == "A"):
+      cfg = dataclasses.replace(cfg, split_k=-1 if mod[2:] == "A" else int(mod[2:]))
+    else:
+      raise KeyError(f"unknown config modifier {mod!r} in {name!r}")
+  return cfg
