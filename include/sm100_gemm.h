@@ -35,7 +35,8 @@ enum {
   BG_ERR_MMA_ACC = 3,    /* MMA issuer timed out waiting for a free accumulator   */
   BG_ERR_EPILOGUE = 4,   /* epilogue timed out waiting for a finished accumulator */
   BG_ERR_DRAIN = 5,      /* final wait for outstanding MMAs timed out             */
-  BG_ERR_LOAD_DRAIN = 6  /* wait for in-flight loads after another error timed out */
+  BG_ERR_LOAD_DRAIN = 6, /* wait for in-flight loads after another error timed out */
+  BG_ERR_SPLIT_K = 7     /* split-K (one wave): a tile's other splits did not all publish in time */
 };
 
 /*
@@ -65,10 +66,11 @@ enum {
  *               clusters with at least 32 k-blocks each; off otherwise).
  *               S in [2, 64] (persistent kernel, tiles a multiple of 32 columns wide, S <= K / 64):
  *               each output tile is computed by S entries of the schedule, each over a contiguous 1/S of K, on
- *               different clusters; every entry writes its fp32 partial sums to a plan-owned workspace and the
- *               entry that finishes last adds them in split order (bitwise reproducible) and writes C; no entry
- *               waits for another. For shapes with few tiles and long K. Not available through bg_gemm_noalloc (it
- *               owns no workspace).
+ *               different clusters; fp32 partial sums meet in a plan-owned workspace and are added in split
+ *               order (bitwise reproducible). When every entry has its own cluster (one wave) the plan launches
+ *               cooperatively and the tile's entries share the reduction out; otherwise the entry that finishes
+ *               last reduces the tile and no entry waits for another. For shapes with few tiles and long K. Not
+ *               available through bg_gemm_noalloc (it owns no workspace).
  */
 typedef struct bg_cfg {
   int32_t kind;

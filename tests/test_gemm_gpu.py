@@ -297,12 +297,15 @@ def _split_k_cases():
     ("one_kblock_each_sk8", WSCfg(BN=64, tma_store=True, split_k=8), (128, 256, 512)),
     ("ragged_pair_sk2", WSCfg(tma_store=True, cluster=2, ragged=True, split_k=2), (300, 520, 1000)),
     ("pair_sk5_few_clusters", WSCfg(cluster=2, split_k=5, num_sm=8), (512, 256, 640)),
+    ("small_ring_sk2", WSCfg(BN=128, stages=3, split_k=2), (256, 512, 1024)),        # reduce through registers
+    ("bm64_reg_sk6", WSCfg(consumers=1, BN=64, split_k=6), (192, 256, 768)),
   ]
 
 
-@pytest.mark.parametrize("idx", range(11))
+@pytest.mark.parametrize("idx", range(13))
 def test_split_k(idx, cuda_dev):
-  """Three launches of one plan on NaN-poisoned C: also checks that every launch leaves the arrival words zero."""
+  """Three launches of one plan on NaN-poisoned C: also checks that every launch leaves the arrival words zero.
+  Single-wave cases reduce through the idle operand ring (cp.async), the others and small rings through registers."""
   from hopper_wgmma import build_gemm_ws
   name, cfg, (M, N, K) = _split_k_cases()[idx]
   worst, launch = run_case(lambda: build_gemm_ws(N, cfg, M, K, wait_budget_ns=BUDGET_NS), M, N, K, cuda_dev)

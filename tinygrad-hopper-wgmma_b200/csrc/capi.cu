@@ -181,6 +181,7 @@ struct bg_plan {
   int threads = 0;
   size_t smem = 0;
   int max_active_clusters = 0;
+  bool cooperative = false;   // split-K with one entry per cluster: all CTAs must be resident at once
   CUtensorMap tmA{}, tmB{}, tmBn{}, tmC{};
   int narrow_tiles = 0;
   GemmParams kp{};
@@ -570,6 +571,8 @@ int32_t setup_plan(const bg_cfg& c, int64_t M, int64_t N, int64_t K, const void*
     p->partial_bytes = static_cast<size_t>(n_entries) * cl * 4u * 32u * static_cast<size_t>(width) * sizeof(float);
     p->ticket_words = static_cast<size_t>(tiles) * cl * 4u;
   }
+  // one entry per cluster: the tile's entries are all resident together (cooperative launch) and share the reduce
+  const bool sk_scatter = sk > 1 && n_entries <= nclusters;
   nclusters = std::min<int64_t>(nclusters, n_entries);
   p->grid = static_cast<int>(nclusters * (c.kind == BG_KIND_RING ? 1 : cl));
 
@@ -618,6 +621,11 @@ int32_t setup_plan(const bg_cfg& c, int64_t M, int64_t N, int64_t K, const void*
   kp.split_k = sk;
   kp.partial = nullptr;
   kp.tickets = nullptr;
+  kp.sk_scatter = sk_scatter ? 1 : 0;
+  // A cooperative launch guarantees that every CTA is resident at once. It cannot be combined with cluster
+  // dimensions here (such a launch fails under Nsight Compute), so CTA pairs rely on the persistent grid being
+  // capped at what the GPU co-schedules, with the bounded wait reporting an error if other work holds SMs.
+  p->cooperative = sk_scatter && cl == 1;
   // split accumulator (two N blocks, one 512-column buffer): how many k-blocks run on half 0 alone at a tile's start
   // and end; it must stay below the ring depth so the producer keeps a free stage
   kp.look = std::max(1, std::min(2, stages - 2));
@@ -756,15 +764,20 @@ int32_t bg_plan_launch(bg_plan* p, void* stream) {
   lc.blockDim = dim3(static_cast<unsigned>(p->threads));
   lc.dynamicSmemBytes = p->smem;
   lc.stream = static_cast<cudaStream_t>(stream);
-  cudaLaunchAttribute at[1];
+  cudaLaunchAttribute at[2];
   lc.attrs = at;
   lc.numAttrs = 0;
   if (p->cl > 1 && p->kind == BG_KIND_WS) {
-    at[0].id = cudaLaunchAttributeClusterDimension;
-    at[0].val.clusterDim.x = p->cl;
-    at[0].val.clusterDim.y = 1;
-    at[0].val.clusterDim.z = 1;
-    lc.numAttrs = 1;
+    at[lc.numAttrs].id = cudaLaunchAttributeClusterDimension;
+    at[lc.numAttrs].val.clusterDim.x = p->cl;
+    at[lc.numAttrs].val.clusterDim.y = 1;
+    at[lc.numAttrs].val.clusterDim.z = 1;
+    ++lc.numAttrs;
+  }
+  if (p->cooperative) {
+    at[lc.numAttrs].id = cudaLaunchAttributeCooperative;
+    at[lc.numAttrs].val.cooperative = 1;
+    ++lc.numAttrs;
   }
   cudaError_t e;
   if (p->kind == BG_KIND_RING)
@@ -790,9 +803,10 @@ int32_t bg_plan_check_error(bg_plan* p, void* stream, uint32_t* err_word) {
     // an interrupted split-K launch can leave arrival words behind; the next launch needs them zero
     if (p->d_tickets) cudaMemset(p->d_tickets, 0, p->ticket_words * sizeof(unsigned int));
     static const char* roles[] = {"?", "producer (free stage)", "MMA (loaded stage)", "MMA (free accumulator)",
-                                  "epilogue (finished accumulator)", "MMA drain", "load drain"};
+                                  "epilogue (finished accumulator)", "MMA drain", "load drain",
+                                  "split-K (partial sums of the tile's other splits)"};
     const uint32_t role = w >> 24;
-    return fail(6, "device wait timed out: %s, counter %u (error word 0x%08x)", role < 7 ? roles[role] : "?",
+    return fail(6, "device wait timed out: %s, counter %u (error word 0x%08x)", role < 8 ? roles[role] : "?",
                 w & 0xFFFFFFu, w);
   }
   return 0;

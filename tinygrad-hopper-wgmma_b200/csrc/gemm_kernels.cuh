@@ -37,6 +37,7 @@ constexpr int kBK = 64;           // K per pipeline stage: one 128-byte swizzle 
 constexpr int kWsThreads = 256;   // warps 0-3 producer / MMA / idle, warps 4-7 epilogue
 constexpr int kRingThreads = 128;
 constexpr int kFirstWave = 160;   // first-wave tile entries passed in the kernel parameters (>= clusters on a B200)
+constexpr int kSkSlots = 8;       // split-K reduce: 4 KB shared-memory slots per epilogue warp (in the idle ring)
 
 // Error word layout: role in bits 24-31, the role's job or tile counter (saturated) in bits 0-23.
 enum : uint32_t {
@@ -46,6 +47,7 @@ enum : uint32_t {
   kErrEpilogue = 4u << 24,    // epilogue timed out waiting for a finished accumulator
   kErrDrain = 5u << 24,       // final wait for outstanding MMAs timed out
   kErrLoadDrain = 6u << 24,   // producer's final wait for its in-flight loads timed out (after another error)
+  kErrSplitK = 7u << 24,      // split-K (one wave): the other entries of a tile did not all publish in time
 };
 
 struct GemmParams {
@@ -84,6 +86,7 @@ struct GemmParams {
   float* partial;          // split-K: fp32 partial sums, one 32-lane x width slice per (entry, CTA of the pair, warp)
   unsigned int* tickets;   // split-K: one arrival word per (tile, CTA of the pair, warp), counting entries whose
                            // partial sums are written; zero between launches
+  int sk_scatter;          // split-K with one entry per cluster, launched cooperatively: the reduce is shared out
   int32_t first_wave[kFirstWave];  // sched[0 .. min(tiles, kFirstWave)) again, delivered with the launch
 };
 
@@ -501,103 +504,6 @@ __global__ void __launch_bounds__(kWsThreads, 1)
     const uint32_t my_stage = sC + static_cast<uint32_t>(q) * 2u * STAGE_C;
     const bool split = NB == 2 && p.acc_bufs == 1;
     uint32_t acc = 0, acc_phase = 0, chunk = 0;
-    // Split-K (p.split_k > 1). The split_k entries of a tile run on different clusters, each into its own
-    // accumulator. Per (tile, CTA, warp) an arrival word counts finished entries: every entry writes its fp32 partial
-    // sums to its own workspace slice, makes them visible at gpu scope and then counts itself. The entry that sees
-    // the count reach split_k - 1 is the last: every other entry's partial sums are visible to it. It adds all
-    // splits in split order (its own from tensor memory), so the rounding does not depend on which entry came last,
-    // stores C and resets the word for the next launch. No entry waits for another.
-    const size_t sk_slice = 32u * static_cast<size_t>(p.bn * NB);                 // floats per slice
-    const size_t sk_stride = static_cast<size_t>(p.cl) * 4u * sk_slice;           // between consecutive splits
-    int sk_own = 0;                  // this entry's split
-    unsigned int* sk_word = nullptr;   // the tile's arrival word for this warp
-    float* sk_src = nullptr;         // this warp's slice of split 0 of the tile
-    // Entry idx's split, arrival word and workspace slices.
-    auto sk_setup = [&](int idx) {
-      const int tile = idx / p.split_k;
-      sk_own = idx - tile * p.split_k;
-      sk_word = p.tickets + (static_cast<size_t>(tile) * p.cl + rank) * 4u + static_cast<size_t>(q);
-      sk_src = p.partial + ((static_cast<size_t>(tile) * p.split_k * p.cl + rank) * 4u + q) * sk_slice;
-    };
-    // Count this entry once all its partial sums are written; true for the last entry of the tile.
-    auto sk_count = [&]() {
-      __threadfence();   // this lane's partial sums are visible at gpu scope before the count
-      __syncwarp();
-      uint32_t prev = 0;
-      if (lane == 0) {
-        prev = atomicAdd(sk_word, 1u);
-        __threadfence();   // acquire: the partial sums counted before this entry are visible from here on
-      }
-      prev = __shfl_sync(0xffffffffu, prev, 0);
-      __syncwarp();
-      const bool last = static_cast<int>(prev) == p.split_k - 1;
-      if (last && lane == 0) atomicExch(sk_word, 0u);   // every split has counted: free for the next launch
-      return last;
-    };
-    // Last entry: replace accumulator columns [0, ncols) at TMEM address tacc (tile-relative columns
-    // [tcol, tcol + ncols)) by the sum over all splits, in place in tensor memory, 32 columns at a time. The other
-    // splits' slices are read in units of 32 columns of one split, two units in flight. Slice layout: float4 g of
-    // lane l at (g * 32 + l) * 4, g = column / 4.
-    auto sk_reduce = [&](uint32_t tacc, int tcol, int ncols) {
-      const int others = p.split_k - 1;
-      const int units = (ncols >> 5) * others;   // unit u: chunk u / others of the (u % others)-th other split
-      auto load = [&](int u, uint32_t (&x)[32]) {
-        const int c = u / others, j = u - c * others;
-        const int s = j < sk_own ? j : j + 1;
-        const float* src = sk_src + static_cast<size_t>(s) * sk_stride +
-                           (static_cast<size_t>((tcol >> 2) + 8 * c) * 32u + static_cast<size_t>(lane)) * 4u;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) ld_global_cg_v4(src + i * 128, x[4 * i], x[4 * i + 1], x[4 * i + 2], x[4 * i + 3]);
-      };
-      float a[32];
-      auto add_own = [&](int c, bool first) {
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(tacc + 32u * c, v);
-        tmem_ld_wait();
-#pragma unroll
-        for (int j = 0; j < 32; ++j) a[j] = first ? __uint_as_float(v[j]) : a[j] + __uint_as_float(v[j]);
-      };
-      // fold unit u (split s of chunk c) into the running sum in the order 0, 1, ..., split_k - 1
-      auto consume = [&](int u, const uint32_t (&x)[32]) {
-        const int c = u / others, j = u - c * others;
-        const int s = j < sk_own ? j : j + 1;
-        if (j == 0 && sk_own == 0) add_own(c, true);
-        else if (j > 0 && sk_own == s - 1) add_own(c, false);
-        const bool first = j == 0 && sk_own != 0;   // split 0 starts the sum
-#pragma unroll
-        for (int e = 0; e < 32; ++e) a[e] = first ? __uint_as_float(x[e]) : a[e] + __uint_as_float(x[e]);
-        if (j == others - 1) {
-          if (sk_own == p.split_k - 1) add_own(c, false);
-          uint32_t v[32];
-#pragma unroll
-          for (int e = 0; e < 32; ++e) v[e] = __float_as_uint(a[e]);
-          tmem_st_32x32b_x32(tacc + 32u * c, v);
-        }
-      };
-      uint32_t xa[32], xb[32];
-      load(0, xa);
-#pragma unroll 1
-      for (int u = 0; u < units; u += 2) {
-        if (u + 1 < units) load(u + 1, xb);
-        consume(u, xa);
-        if (u + 2 < units) load(u + 2, xa);
-        if (u + 1 < units) consume(u + 1, xb);
-      }
-      tmem_st_wait();
-    };
-    // Write accumulator columns [0, ncols) at TMEM address tacc (tile-relative columns [tcol, tcol + ncols)) as fp32
-    // into the slice `dst`.
-    auto put_partial = [&](uint32_t tacc, int tcol, int ncols, float* dst) {
-      float* d = dst + (static_cast<size_t>(tcol >> 2) * 32u + static_cast<size_t>(lane)) * 4u;
-#pragma unroll 1
-      for (int c = 0; c < (ncols >> 5); ++c) {
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(tacc + 32u * c, v);
-        tmem_ld_wait();
-#pragma unroll
-        for (int i = 0; i < 8; ++i) st_global_v4(d + (8 * c + i) * 128, v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
-      }
-    };
     // Write accumulator columns starting at TMEM address tacc (this warp's lanes) to C rows row0.., columns
     // [ccol, ccol + ncols).
     auto drain = [&](uint32_t tacc, int row0, int ccol, int ncols) {
@@ -649,6 +555,205 @@ __global__ void __launch_bounds__(kWsThreads, 1)
           mbar_arrive_local(bar);
       }
     };
+    // Split-K (p.split_k > 1). The split_k entries of a tile run on different clusters, each into its own
+    // accumulator, and meet through a workspace of fp32 slices (one per entry, CTA of the pair and warp; 32 lanes x
+    // width columns, float4 g = column / 4 of lane l at (g * 32 + l) * 4) and one arrival word per (tile, CTA, warp).
+    // The sum over the splits is always taken in split order 0, 1, ..., split_k - 1 (an entry's own values from its
+    // tensor memory, in their place), so the rounding does not depend on the order in which the entries finish.
+    //   * one wave (p.sk_scatter: every entry on its own cluster, all resident at once under a cooperative launch):
+    //     the tile's 32-column chunks are shared out among its entries. Each entry publishes the chunks the others
+    //     reduce, counts itself, waits (bounded) until all split_k entries have counted, then reduces its own chunks
+    //     and stores them to C; a second count lets the last entry through reset the word.
+    //   * otherwise: every entry publishes all its chunks and counts itself; the entry that sees the count reach
+    //     split_k - 1 is the last, reduces the whole tile into its tensor memory, drains it as usual and resets the
+    //     word. No entry waits for another.
+    const size_t sk_slice = 32u * static_cast<size_t>(p.bn * NB);                 // floats per slice
+    const size_t sk_stride = static_cast<size_t>(p.cl) * 4u * sk_slice;           // between consecutive splits
+    int sk_own = 0;                    // this entry's split
+    unsigned int* sk_word = nullptr;   // the tile's arrival word for this warp
+    float* sk_src = nullptr;           // this warp's slice of split 0 of the tile
+    auto sk_setup = [&](int idx) {
+      const int tile = idx / p.split_k;
+      sk_own = idx - tile * p.split_k;
+      sk_word = p.tickets + (static_cast<size_t>(tile) * p.cl + rank) * 4u + static_cast<size_t>(q);
+      sk_src = p.partial + ((static_cast<size_t>(tile) * p.split_k * p.cl + rank) * 4u + q) * sk_slice;
+    };
+    // Publish accumulator chunks [0, nch) except [skip_lo, skip_hi) (chunk c = 32 columns at TMEM tacc + 32 c).
+    auto sk_publish = [&](uint32_t tacc, int nch, int skip_lo, int skip_hi) {
+      float* d = sk_src + static_cast<size_t>(sk_own) * sk_stride + static_cast<size_t>(lane) * 4u;
+#pragma unroll 1
+      for (int c = 0; c < nch; ++c) {
+        if (c >= skip_lo && c < skip_hi) continue;
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(tacc + 32u * c, v);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 8; ++i) st_global_v4(d + (8 * c + i) * 128, v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+      }
+      __threadfence();   // this lane's partial sums are visible at gpu scope before the count
+      __syncwarp();
+    };
+    // Last-arrival protocol: count this entry; true for the last entry of the tile (which then resets the word).
+    auto sk_count = [&]() {
+      uint32_t prev = 0;
+      if (lane == 0) {
+        prev = atomicAdd(sk_word, 1u);
+        __threadfence();   // acquire: the partial sums counted before this entry are visible from here on
+      }
+      prev = __shfl_sync(0xffffffffu, prev, 0);
+      __syncwarp();
+      const bool last = static_cast<int>(prev) == p.split_k - 1;
+      if (last && lane == 0) atomicExch(sk_word, 0u);   // every split has counted: free for the next launch
+      return last;
+    };
+    // Scatter protocol: count this entry, then wait until every entry of the tile has counted. False on timeout.
+    auto sk_count_all = [&](int i) {
+      bool ok = true;
+      if (lane == 0) {
+        atomicAdd(sk_word, 1u);
+        const uint32_t all = static_cast<uint32_t>(p.split_k);
+        if (ld_acquire_gpu(sk_word) < all) {
+          const uint64_t t0 = globaltimer_ns();
+          while (ld_acquire_gpu(sk_word) < all) {
+            if (globaltimer_ns() - t0 > budget) {
+              ok = false;
+              break;
+            }
+            __nanosleep(32);
+          }
+        }
+        __threadfence();
+        if (!ok) record_error(p.err, kErrSplitK, i);
+      }
+      ok = __shfl_sync(0xffffffffu, ok ? 1u : 0u, 0) != 0;
+      __syncwarp();
+      return ok;
+    };
+    // Scatter protocol, after the reduce: the last of the tile's 2 * split_k counts resets the word.
+    auto sk_leave = [&]() {
+      __syncwarp();
+      if (lane == 0 && atomicAdd(sk_word, 1u) == 2u * static_cast<uint32_t>(p.split_k) - 1u) atomicExch(sk_word, 0u);
+    };
+    // Reduce chunks [c_begin, c_end) of the tile over all splits. Each finished chunk goes back into tensor memory
+    // or, with `crow` set, is rounded and stored to C row crow (columns 32 c onwards; `cols_left` columns of C
+    // from the tile's first, `row_ok` false for rows outside C). The other splits' slices are read in units of one
+    // chunk of one split (4 KB per warp). With `staged` (the operand ring is idle: this is the cluster's last
+    // entry and its accumulator is complete) each warp streams units through kSkSlots 4 KB slots of the ring with
+    // cp.async, every lane copying and reading back only its own 16-byte pieces; otherwise two units at a time go
+    // through registers (one at a time for wide tiles).
+    auto sk_reduce = [&](uint32_t tacc, int c_begin, int c_end, bool staged, __nv_bfloat16* crow, bool row_ok,
+                         int cols_left) {
+      const int others = p.split_k - 1;
+      const int units = (c_end - c_begin) * others;   // unit u: chunk c_begin + u / others, (u % others)-th other split
+      auto src_of = [&](int u) {
+        const int c = c_begin + u / others, j = u % others;
+        const int s = j < sk_own ? j : j + 1;
+        return sk_src + static_cast<size_t>(s) * sk_stride + (static_cast<size_t>(8 * c) * 32u + static_cast<size_t>(lane)) * 4u;
+      };
+      auto load = [&](int u, uint32_t (&x)[32]) {
+        const float* src = src_of(u);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) ld_global_cg_v4(src + i * 128, x[4 * i], x[4 * i + 1], x[4 * i + 2], x[4 * i + 3]);
+      };
+      float a[32];
+      auto add_own = [&](int c, bool first) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(tacc + 32u * c, v);
+        tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 32; ++j) a[j] = first ? __uint_as_float(v[j]) : a[j] + __uint_as_float(v[j]);
+      };
+      // fold unit u (split s of chunk c) into the running sum in the order 0, 1, ..., split_k - 1
+      auto consume = [&](int u, const uint32_t (&x)[32]) {
+        const int c = c_begin + u / others, j = u % others;
+        const int s = j < sk_own ? j : j + 1;
+        if (j == 0 && sk_own == 0) add_own(c, true);
+        else if (j > 0 && sk_own == s - 1) add_own(c, false);
+        const bool first = j == 0 && sk_own != 0;   // split 0 starts the sum
+#pragma unroll
+        for (int e = 0; e < 32; ++e) a[e] = first ? __uint_as_float(x[e]) : a[e] + __uint_as_float(x[e]);
+        if (j == others - 1) {
+          if (sk_own == p.split_k - 1) add_own(c, false);
+          uint32_t v[32];
+#pragma unroll
+          for (int e = 0; e < 32; ++e) v[e] = __float_as_uint(a[e]);
+          if (crow == nullptr) {
+            tmem_st_32x32b_x32(tacc + 32u * c, v);
+          } else if (row_ok) {
+            const int cols = cols_left - 32 * c;
+            if (cols >= 32) store_row_global<32>(crow + 32 * c, v);
+            else if (cols > 0) store_row_global_masked<32>(crow + 32 * c, v, cols);
+          }
+        }
+      };
+      if (staged) {
+        const uint32_t wbase = sA + static_cast<uint32_t>(q) * (kSkSlots * 4096u) + static_cast<uint32_t>(lane) * 16u;
+        auto issue = [&](int u) {   // one commit group per unit, empty past the end, so that groups stay in step
+          if (u < units) {
+            const float* src = src_of(u);
+            const uint32_t dst = wbase + static_cast<uint32_t>(u % kSkSlots) * 4096u;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) cp_async_16(dst + i * 512u, src + i * 128);
+          }
+          cp_async_commit();
+        };
+#pragma unroll 1
+        for (int u = 0; u < kSkSlots; ++u) issue(u);
+#pragma unroll 1
+        for (int u = 0; u < units; ++u) {
+          cp_async_wait<kSkSlots - 1>();   // unit u has landed
+          uint32_t x[32];
+          const uint32_t slot = wbase + static_cast<uint32_t>(u % kSkSlots) * 4096u;
+#pragma unroll
+          for (int i = 0; i < 8; ++i) ld_shared_v4(slot + i * 512u, x[4 * i], x[4 * i + 1], x[4 * i + 2], x[4 * i + 3]);
+          consume(u, x);   // uses x, so the slot has been read before it is refilled below
+          issue(u + kSkSlots);
+        }
+        cp_async_wait<0>();
+      } else if constexpr (NB == 1) {
+        uint32_t xa[32], xb[32];
+        if (units > 0) load(0, xa);
+#pragma unroll 1
+        for (int u = 0; u < units; u += 2) {
+          if (u + 1 < units) load(u + 1, xb);
+          consume(u, xa);
+          if (u + 2 < units) load(u + 2, xa);
+          if (u + 1 < units) consume(u + 1, xb);
+        }
+      } else {   // wide tiles: one unit at a time (their kernels have no registers to spare for two)
+#pragma unroll 1
+        for (int u = 0; u < units; ++u) {
+          uint32_t x[32];
+          load(u, x);
+          consume(u, x);
+        }
+      }
+    };
+    // The operand ring can stage the reduce: big enough for every warp's slots, and idle after the accumulator of
+    // the cluster's last entry is complete (no loads follow, and the MMAs that read it have finished).
+    const bool sk_ring_ok =
+        static_cast<uint32_t>(p.stages) * (p.a_stage_bytes + p.b_stage_bytes) >= 4u * kSkSlots * 4096u;
+    // The split-K epilogue of entry idx, whose accumulator (nch chunks at TMEM tacc) is complete. False on timeout.
+    auto sk_epilogue = [&](int idx, int i, uint32_t tacc, int nch, int row0, int col0) {
+      sk_setup(idx);
+      const bool staged = sk_ring_ok && idx + p.nclusters >= p.tiles;
+      if (p.sk_scatter) {
+        const int lo = sk_own * nch / p.split_k, hi = (sk_own + 1) * nch / p.split_k;
+        sk_publish(tacc, nch, lo, hi);
+        if (!sk_count_all(i)) return false;
+        sk_reduce(tacc, lo, hi, staged, p.C + static_cast<long long>(row0 + lane) * p.ldc + col0,
+                  lane < ROWS_W && row0 + lane < p.m_valid, p.n_valid - col0);
+        sk_leave();
+        return true;
+      }
+      sk_publish(tacc, nch, 0, 0);
+      if (sk_count()) {
+        sk_reduce(tacc, 0, nch, staged, nullptr, false, 0);
+        tmem_st_wait();
+        drain(tacc, row0, col0, nch * 32);
+      }
+      return true;
+    };
     for (int i = 0;; ++i) {
       const int idx = cid + i * p.nclusters;
       if (idx >= p.tiles) break;
@@ -669,26 +774,16 @@ __global__ void __launch_bounds__(kWsThreads, 1)
             break;
           }
           tc_fence_after();
+          if (SPLITK && p.split_k > 1) continue;   // both halves first, then the split-K epilogue on the whole tile
           const uint32_t tacc = tmem_base + lane_base + static_cast<uint32_t>(h * p.bn);
-          if (SPLITK && p.split_k > 1) {
-            if (h == 0) sk_setup(idx);
-            put_partial(tacc, h * p.bn, p.bn, sk_src + static_cast<size_t>(sk_own) * sk_stride);
-            continue;
-          }
           if (h == 0 || !narrow) drain(tacc, row0, col0 + h * p.bn, p.bn);
           release(tempty0 + 8u * h);
         }
         if (!ok) break;
         if (SPLITK && p.split_k > 1) {
-          const bool last = sk_count();
-          for (int h = 0; h < 2; ++h) {
-            const uint32_t tacc = tmem_base + lane_base + static_cast<uint32_t>(h * p.bn);
-            if (last) {
-              sk_reduce(tacc, h * p.bn, p.bn);
-              drain(tacc, row0, col0 + h * p.bn, p.bn);
-            }
-            release(tempty0 + 8u * h);
-          }
+          if (!sk_epilogue(idx, i, tmem_base + lane_base, width >> 5, row0, col0)) break;
+          release(tempty0);
+          release(tempty0 + 8u);
         }
         acc_phase ^= 1u;
         continue;
@@ -700,12 +795,7 @@ __global__ void __launch_bounds__(kWsThreads, 1)
       tc_fence_after();
       const uint32_t tacc = tmem_base + lane_base + acc * static_cast<uint32_t>(p.acc_stride);
       if (SPLITK && p.split_k > 1) {
-        sk_setup(idx);
-        put_partial(tacc, 0, width, sk_src + static_cast<size_t>(sk_own) * sk_stride);
-        if (sk_count()) {
-          sk_reduce(tacc, 0, width);
-          drain(tacc, row0, col0, width);
-        }
+        if (!sk_epilogue(idx, i, tacc, width >> 5, row0, col0)) break;
       } else {
         drain(tacc, row0, col0, width);
       }

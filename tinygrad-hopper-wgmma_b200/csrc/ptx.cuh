@@ -172,9 +172,33 @@ __device__ __forceinline__ void st_global_v4(void* ptr, uint32_t a, uint32_t b, 
 }
 
 // Split-K partial sums travel between SMs within one launch: their loads go through L2 only (.cg), since L1 is
-// not coherent across SMs.
+// not coherent across SMs. cp_async_16 is the asynchronous form (global -> this CTA's shared memory, 16 bytes, no
+// registers held while in flight); each commit closes a group, and wait_group<N> returns once at most N of this
+// thread's groups are still in flight, after which the thread sees the data it copied.
 __device__ __forceinline__ void ld_global_cg_v4(const void* ptr, uint32_t& a, uint32_t& b, uint32_t& c, uint32_t& d) {
   asm volatile("ld.global.cg.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(a), "=r"(b), "=r"(c), "=r"(d) : "l"(ptr) : "memory");
+}
+
+// gpu-scope acquire load of a split-K arrival word.
+__device__ __forceinline__ uint32_t ld_acquire_gpu(const unsigned int* ptr) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(ptr) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void cp_async_16(uint32_t smem_dst, const void* gmem_src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_dst), "l"(gmem_src) : "memory");
+}
+
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+__device__ __forceinline__ void ld_shared_v4(uint32_t addr, uint32_t& a, uint32_t& b, uint32_t& c, uint32_t& d) {
+  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(a), "=r"(b), "=r"(c), "=r"(d) : "r"(addr) : "memory");
 }
 
 // ---------------------------------------------------------------------------------------------------------------

@@ -78,7 +78,8 @@ def ncu_sweep(reps: int, out, jobs=None) -> None:
                             capture_output=True, text=True, env=env)
       text = log.read_text() if log.exists() else ""
     if prof.returncode != 0 or not text:
-      print(f"ERROR {m}x{n}x{k}: ncu exited {prof.returncode}", file=out, flush=True)
+      tail = " | ".join((prof.stdout + prof.stderr).strip().splitlines()[-4:])
+      print(f"ERROR {m}x{n}x{k}: ncu exited {prof.returncode}: {tail[-400:]}", file=out, flush=True)
       continue
     rows = list(ncu_table._rows(text))
     ours = [us for name, us in rows if "sm100_gemm" in name]
