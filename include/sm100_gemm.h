@@ -71,6 +71,9 @@ enum {
  *               cooperatively and the tile's entries share the reduction out; otherwise the entry that finishes
  *               last reduces the tile and no entry waits for another. For shapes with few tiles and long K. Not
  *               available through bg_gemm_noalloc (it owns no workspace).
+ *   no_k_serpentine 0 (default): a persistent cluster walks K forwards on its even-numbered tiles and backwards on
+ *               its odd-numbered ones, so each wave starts on the K-slabs the previous wave left in L2 (fewer DRAM
+ *               reads); 1: always forwards (the fp32 accumulation order of every tile then runs along K)
  */
 typedef struct bg_cfg {
   int32_t kind;
@@ -91,6 +94,7 @@ typedef struct bg_cfg {
   int32_t no_tail_split;
   int32_t ragged;
   int32_t split_k;
+  int32_t no_k_serpentine;
 } bg_cfg;
 
 /* What a plan resolved to (for reports and tests). */

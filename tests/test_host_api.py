@@ -40,14 +40,14 @@ def test_library_reports_missing_device_as_runtime_error_not_crash():
 
 
 def test_cfg_struct_layout_matches_header():
-  """The ctypes mirror of bg_cfg has the header's fields in order (12 int32, int64, 5 int32, padded to 8 bytes)."""
+  """The ctypes mirror of bg_cfg has the header's fields in order (12 int32, int64, 6 int32)."""
   import ctypes
   from hopper_wgmma import _capi
   text = (ROOT / "include" / "sm100_gemm.h").read_text()
   body = text[text.index("typedef struct bg_cfg {"):text.index("} bg_cfg;")]
   fields = re.findall(r"int(?:32|64)_t\s+(\w+);", body)
   assert [f for f, _ in _capi.BgCfg._fields_] == fields
-  assert ctypes.sizeof(_capi.BgCfg) == 12 * 4 + 8 + 5 * 4 + 4
+  assert ctypes.sizeof(_capi.BgCfg) == 12 * 4 + 8 + 6 * 4
 
 
 # ----------------------------------------------------------------------------------------------------------------

@@ -622,6 +622,7 @@ int32_t setup_plan(const bg_cfg& c, int64_t M, int64_t N, int64_t K, const void*
   kp.partial = nullptr;
   kp.tickets = nullptr;
   kp.sk_scatter = sk_scatter ? 1 : 0;
+  kp.k_serpentine = c.no_k_serpentine ? 0 : 1;
   // A cooperative launch guarantees that every CTA is resident at once. It cannot be combined with cluster
   // dimensions here (such a launch fails under Nsight Compute), so CTA pairs rely on the persistent grid being
   // capped at what the GPU co-schedules, with the bounded wait reporting an error if other work holds SMs.

@@ -87,6 +87,7 @@ struct GemmParams {
   unsigned int* tickets;   // split-K: one arrival word per (tile, CTA of the pair, warp), counting entries whose
                            // partial sums are written; zero between launches
   int sk_scatter;          // split-K with one entry per cluster, launched cooperatively: the reduce is shared out
+  int k_serpentine;        // a cluster walks K backwards on its odd-numbered tiles (1) or always forwards (0)
   int32_t first_wave[kFirstWave];  // sched[0 .. min(tiles, kFirstWave)) again, delivered with the launch
 };
 
@@ -277,7 +278,12 @@ __global__ void __launch_bounds__(kWsThreads, 1)
       const int row_b = tn * width + (PAIRED ? static_cast<int>(rank) * (bsub / 2) : 0);
       int kb0, nk;
       k_range<SPLITK>(p, idx, kb0, nk);
+      // K serpentine: consecutive tiles of a cluster walk K in opposite directions, so a wave of tiles starts on
+      // the K-slabs the previous wave read last, which are still in L2 (fewer DRAM reads, less power under the
+      // cap). The MMA side counts k-blocks from the first one issued, whichever the direction.
+      const bool reverse = p.k_serpentine != 0 && (i & 1) != 0;
       for (int kb = kb0; kb < kb0 + nk; ++kb, ++job) {
+        const int kc = reverse ? 2 * kb0 + nk - 1 - kb : kb;   // the k-block this job loads
         if (!mbar_wait_warp(empty0 + 8u * stage, phase ^ 1u, budget)) {
           if (lane == 0) record_error(p.err, kErrProducer, job);
           failed = true;
@@ -290,16 +296,16 @@ __global__ void __launch_bounds__(kWsThreads, 1)
           if (PAIRED) {
             const uint32_t fb_leader = mapa_shared(fb, 0);
             if (leader) mbar_arrive_expect_tx(fb, tx);
-            tma_load_2d_pair(a_dst, &tmA, fb_leader, kb * kBK, row_a);
+            tma_load_2d_pair(a_dst, &tmA, fb_leader, kc * kBK, row_a);
 #pragma unroll
             for (int nb = 0; nb < NB; ++nb)
-              if (nb < nblk) tma_load_2d_pair(b_dst + nb * p.b_block_bytes, mapB, fb_leader, kb * kBK, row_b + nb * bsub);
+              if (nb < nblk) tma_load_2d_pair(b_dst + nb * p.b_block_bytes, mapB, fb_leader, kc * kBK, row_b + nb * bsub);
           } else {
             mbar_arrive_expect_tx(fb, tx);
-            tma_load_2d(a_dst, &tmA, fb, kb * kBK, row_a);
+            tma_load_2d(a_dst, &tmA, fb, kc * kBK, row_a);
 #pragma unroll
             for (int nb = 0; nb < NB; ++nb)
-              if (nb < nblk) tma_load_2d(b_dst + nb * p.b_block_bytes, mapB, fb, kb * kBK, row_b + nb * bsub);
+              if (nb < nblk) tma_load_2d(b_dst + nb * p.b_block_bytes, mapB, fb, kc * kBK, row_b + nb * bsub);
           }
         }
         __syncwarp();

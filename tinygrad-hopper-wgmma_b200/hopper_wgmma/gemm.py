@@ -146,6 +146,7 @@ class WSCfg:
   ragged: bool = False         # accept any M (and N, K multiples of 8): edge tiles are zero-filled / clipped
   split_k: int = 1             # K splits per output tile (fp32 partial sums reduced in-kernel by the last split);
                                # -1 = chosen per shape (only shapes with few tiles and long K are split)
+  k_serpentine: bool = True    # alternate the K direction from tile to tile of a cluster (L2 reuse across waves)
 
   def __post_init__(self):
     if self.BK != 64: raise ValueError("BK must be 64 (one 128-byte swizzle atom)")
@@ -199,7 +200,8 @@ class WSCfg:
     return (f"ws_c{self.consumers}_s{st}_n{self.BN}_sm{sm}_g{self.group_m}x{self.group_n}"
             f"{'_tmast' if self.tma_store else ''}{'_hil' if self.hilbert else ''}"
             f"{f'_r{self.regs[0]}x{self.regs[1]}' if self.regs else ''}{f'_cl{self.cluster}' if self.cluster > 1 else ''}"
-            f"{f'_x{self.n_mma}' if self.n_mma > 1 else ''}{f'_sk{self.split_k}' if self.split_k > 1 else '_skA' if self.split_k == -1 else ''}")
+            f"{f'_x{self.n_mma}' if self.n_mma > 1 else ''}{f'_sk{self.split_k}' if self.split_k > 1 else '_skA' if self.split_k == -1 else ''}"
+            f"{'' if self.k_serpentine else '_kfwd'}")
 
   def to_c(self, kind: int = _capi.KIND_WS, num_sm: int | None = None, wait_budget_ns: int = 0,
            debug_skip_job: int = -1) -> _capi.BgCfg:
@@ -208,7 +210,7 @@ class WSCfg:
                        tma_store=int(self.tma_store), cluster=self.cluster, hilbert=int(self.hilbert),
                        acc_bufs=self.acc_bufs or 0, wait_budget_ns=wait_budget_ns, debug_skip_job=debug_skip_job,
                        n_mma=self.n_mma, no_tail_split=0 if self.split_tail else 1, ragged=int(self.ragged),
-                       split_k=self.split_k)
+                       split_k=self.split_k, no_k_serpentine=0 if self.k_serpentine else 1)
 
 
 # =============================================================================================================
