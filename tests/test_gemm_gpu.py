@@ -48,16 +48,6 @@ def fp32_product(A, B):
     torch.backends.cuda.matmul.allow_tf32 = tf32
 
 
-def max_bf16_ulps(ours, ref):
-  """Largest elementwise |ours - ref| in units of the bf16 spacing at the larger magnitude of the pair. Two correct
-  results that differ only in fp32 summation order round to the same or an adjacent bf16 value (<= 1)."""
-  torch = _torch()
-  a, b = ours.float(), ref.float()
-  _, e = torch.frexp(torch.maximum(a.abs(), b.abs()))
-  ulp = torch.ldexp(torch.ones_like(a), e - 8)   # values in [2^(e-1), 2^e) step by 2^(e-8) in bf16
-  return float(((a - b).abs() / ulp).max())
-
-
 def inputs(M, N, K, seed=0):
   from oracle import gemm_ref
   return gemm_ref.randn_bf16_bits((M, K), seed), gemm_ref.randn_bf16_bits((K, N), seed + 1)
@@ -164,8 +154,9 @@ def test_b200_cases(idx, cuda_dev):
 
 def test_matches_cublas_bitwise_or_close(cuda_dev):
   """Against torch.matmul (cuBLAS) on the same bf16 inputs: the reference printed rel=0.00000 for every CHECK
-  (scripts/ncu_workload.py:60-64). Both accumulate in fp32, so every element equals cuBLAS's or is its bf16
-  neighbour, and most are equal."""
+  (scripts/ncu_workload.py:60-64). Both accumulate in fp32 and round to bf16, so most elements are bitwise equal;
+  the summation order differs, so elements near zero or on a rounding boundary may not be. Parity itself is
+  measured against the fp32 product."""
   torch = _torch()
   from hopper_wgmma import WSCfg, build_gemm_ws
   g = torch.Generator(device=cuda_dev).manual_seed(0)
@@ -177,9 +168,7 @@ def test_matches_cublas_bitwise_or_close(cuda_dev):
   launch()
   launch.check()
   assert not torch.isnan(C).any()
-  cub = A @ B
-  assert max_bf16_ulps(C, cub) <= 1.0
-  assert float((C == cub).float().mean()) >= 0.9
+  assert float((C == A @ B).float().mean()) >= 0.9
   ref = fp32_product(A, B)
   rel = float((C.float() - ref).abs().max() / (ref.abs().max() + 1e-9))
   assert rel <= TOL, rel
@@ -262,7 +251,7 @@ def test_contract_errors_before_launch(cuda_dev):
 @pytest.mark.parametrize("size,cfg_name", [(4096, "cluster_hilbert"), (8192, "cluster_hilbert"), (4096, "tma_store")])
 def test_full_size_sampled(size, cfg_name, cuda_dev):
   """Headline sizes: 64 sampled rows against the fp32 CPU oracle, every element against the fp32 product on the GPU
-  (cuBLAS, TF32 off) and within one bf16 step of cuBLAS's bf16 output, NaN scan."""
+  (cuBLAS, TF32 off), NaN scan."""
   torch = _torch()
   from hopper_wgmma.ladder import LADDER, build
   from oracle import gemm_ref
@@ -282,7 +271,6 @@ def test_full_size_sampled(size, cfg_name, cuda_dev):
   ref = fp32_product(A, B)
   rel = float((C.float() - ref).abs().max() / (ref.abs().max() + 1e-9))
   assert rel <= TOL, rel
-  assert max_bf16_ulps(C, A @ B) <= 1.0
 
 
 # ------------------------------------------------------------------------------------------------------------------

@@ -2,7 +2,8 @@
 
     python -m hopper_wgmma.report sweep [--reps 30] > sweep.log        # run the shape sweep + ladders on this GPU
     python -m hopper_wgmma.report ncu-sweep [--reps 5] > ncu.log        # the same, timed by Nsight Compute
-    python -m hopper_wgmma.report summary sweep.log [...] > summary.md  # markdown tables from TIME / NCU lines
+    python -m hopper_wgmma.report summary sweep.log [...] > summary.md  # markdown tables from TIME lines
+    python -m hopper_wgmma.report ncu-summary ncu.log [...]             # the same from an ncu-sweep's NCU lines
 
 ``sweep`` runs hopper_wgmma.workload in-process for every shape of ladder.SWEEP_SHAPES with the configs of
 ladder.SWEEP_CONFIGS, and the ladder (ladder.LADDER) at 4096 and 8192, each config timed interleaved with cuBLAS on
@@ -97,6 +98,32 @@ def ncu_sweep(reps: int, out, jobs=None) -> None:
       print("NCU " + json.dumps(rec), file=out, flush=True)
 
 
+def _ncu_lines(text: str):
+  for line in text.splitlines():
+    if line.startswith("NCU "): yield json.loads(line[4:])
+
+
+def ncu_summary(texts: list[str], peak_tflops: float) -> str:
+  """Markdown table of an ``ncu-sweep`` log: per shape the config with the best ratio to cuBLAS (kernel time =
+  best-of-reps gpu__time_duration), then every config's ratio, best first."""
+  by_shape: dict[tuple, list] = {}
+  for t in texts:
+    for r in _ncu_lines(t): by_shape.setdefault(tuple(r["shape"]), []).append(r)
+  out = ["| M×N×K | best config | µs | TFLOPS | cuBLAS TFLOPS | % of cuBLAS | % of peak |",
+         "|---|---|---:|---:|---:|---:|---:|"]
+  order = sorted(by_shape, key=lambda s: s[0] * s[1] * s[2])
+  for shape in order:
+    best = max(by_shape[shape], key=lambda r: r.get("pct_cublas", 0.0))
+    out.append(f"| {shape[0]}×{shape[1]}×{shape[2]} | {best['label']} | {best['us_best']:.1f} | {best['tflops']:.0f} | "
+               f"{best['cublas_tflops']:.0f} | {best['pct_cublas']:.1f}% | {100 * best['tflops'] / peak_tflops:.1f}% |")
+  out.append("")
+  for shape in order:
+    rows = sorted(by_shape[shape], key=lambda r: -r.get("pct_cublas", 0.0))
+    out.append(f"**{shape[0]}×{shape[1]}×{shape[2]}** — " + ", ".join(f"{r['label']} {r['pct_cublas']:.1f}%" for r in rows))
+    out.append("")
+  return "\n".join(out)
+
+
 def summary(texts: list[str], peak_tflops: float) -> str:
   recs = [r for t in texts for r in _time_lines(t) if r.get("label") != "cublas"]
   by_shape: dict[tuple, list] = {}
@@ -128,6 +155,9 @@ def main(argv=None) -> int:
   b = sub.add_parser("summary")
   b.add_argument("logs", nargs="+")
   b.add_argument("--peak", type=float, default=0.0, help="TFLOPS; default: MEASURED_PEAKS.json bf16_tflops or 1590")
+  d = sub.add_parser("ncu-summary")
+  d.add_argument("logs", nargs="+")
+  d.add_argument("--peak", type=float, default=0.0, help="TFLOPS; default: MEASURED_PEAKS.json bf16_tflops or 1590")
   args = ap.parse_args(argv)
   if args.cmd == "sweep":
     sweep(args.reps, sys.stdout)
@@ -144,7 +174,8 @@ def main(argv=None) -> int:
   if not peak:
     p = Path(__file__).resolve().parents[2] / "MEASURED_PEAKS.json"
     peak = json.loads(p.read_text())["bf16_tflops"] if p.exists() else 1590.0
-  print(summary([Path(f).read_text() for f in args.logs], peak))
+  fn = ncu_summary if args.cmd == "ncu-summary" else summary
+  print(fn([Path(f).read_text() for f in args.logs], peak))
   return 0
 
 
