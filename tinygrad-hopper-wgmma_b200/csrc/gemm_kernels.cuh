@@ -1,5 +1,6 @@
 // bf16 GEMM kernels for sm_100a: C[M,N] = A[M,K] * B[K,N], operands K-major (A row-major, B given as BT[N,K]),
-// fp32 accumulation in tensor memory, bf16 output, every dimension a multiple of the tile.
+// fp32 accumulation in tensor memory, bf16 output. Shapes are tile multiples unless the host asks for ragged edges
+// (TMA zero-fills loads past the operands; stores are clipped or masked).
 //
 //   sm100_gemm_ws    warp-specialized tcgen05 GEMM. Used for the reference's persistent ladder rungs
 //                    (hopper_wgmma/gemm.py:293-398: role_split, tma_store, hilbert, cluster, cluster_hilbert) with
@@ -24,6 +25,9 @@
 // In a CTA pair (PAIRED, cta_group::2) both CTAs load their own A rows and their own half of the B tile; only the
 // even CTA issues MMAs (M = 256 across the pair); the odd CTA's loads complete on the even CTA's barriers and the
 // MMA commits arrive on both CTAs' barriers. No load is multicast.
+// A persistent cluster walks K forwards on its even-numbered tiles and backwards on its odd-numbered ones (K
+// serpentine), and with SPLITK = true the tile table may hold several entries per tile over disjoint K ranges, whose
+// fp32 partial sums the epilogue warps combine through a global workspace (see the split-K block of the epilogue).
 //
 // Every mbarrier wait is bounded (GemmParams::budget_ns). On expiry a thread writes a code into GemmParams::err and
 // leaves its loop; all other roles then run out of work or time out too, the kernel drains what it issued, frees
