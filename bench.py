@@ -189,13 +189,19 @@ def run_reference(args):
 # ------------------------------------------------------------------------------------------------------------------
 # our arm
 # ------------------------------------------------------------------------------------------------------------------
-def pick_cfg(name: str):
+def pick_cfg(name: str, m: int, n: int):
+  """``best`` = the fastest config of the ncu shape sweep for this size of per-rank GEMM: 256x256 CTA-pair tiles up to
+  about 6144^2 outputs, 256x512 pair tiles (two N = 256 MMAs per K step) from 8192^2 outputs up. Any other name is
+  looked up in the ladder tables (``hopper_wgmma.ladder.lookup``, modifiers such as ``@skA`` included)."""
   from hopper_wgmma import WSCfg
-  from hopper_wgmma.ladder import LADDER, SWEEP
-  if name == "best": return "best", WSCfg(tma_store=True, cluster=2, hilbert=True)
-  table = {**LADDER, **SWEEP}
-  if name not in table: raise SystemExit(f"unknown --cfg {name}; choose from best, {', '.join(table)}")
-  return name, table[name]
+  from hopper_wgmma.ladder import lookup
+  if name == "best":
+    if m * n >= 8192 * 8192: return "best", WSCfg(tma_store=True, cluster=2, n_mma=2, hilbert=True)
+    return "best", WSCfg(tma_store=True, cluster=2, hilbert=True)
+  try:
+    return name, lookup(name)
+  except (KeyError, ValueError) as exc:
+    raise SystemExit(f"unknown --cfg {name}: {exc}")
 
 
 def run_ours(args):
@@ -218,7 +224,7 @@ def run_ours(args):
     if world > 1: dist.barrier()
 
   M, n, K, N_total, scaling = shapes(args.workload, world)
-  cfg_name, cfg = pick_cfg(args.cfg)
+  cfg_name, cfg = pick_cfg(args.cfg, M, n)
   flops_rank = 2.0 * M * n * K
 
   # inputs resident in HBM: A replicated (same seed everywhere), this rank's K-major B shard, this rank's C shard
@@ -373,7 +379,8 @@ def run_ours(args):
     dist.barrier()
     dist.destroy_process_group()
   if rank != 0: return
-  tag = f"sm100_gemm_ws_{'pair' if info['paired'] else 'cta'}_{'tmast' if cfg.tma_store else 'reg'}"
+  tag = (f"sm100_gemm_ws_{'pair' if info['paired'] else 'cta'}_{'tmast' if cfg.tma_store else 'reg'}"
+         f"{'_x2' if cfg.n_mma == 2 else ''}")
   traffic = profiled_traffic(tag, args.workload, flops_rank)
   line = {
     "metric": METRIC, "value": round(value, 3), "unit": "TFLOPS", "n_gpus": world, "steps": args.steps,
