@@ -555,7 +555,12 @@ __global__ void __launch_bounds__(kWsThreads, 1)
         epilogue_registers(tacc, crow, ncols, lane < ROWS_W && row0 + lane < p.m_valid, p.n_valid - ccol);
       }
     };
+    // Free an accumulator buffer for the MMA warp. The cluster's last entry skips it: no MMA waits for that buffer
+    // again, and in a pair the remote arrive would only delay the teardown (tensor memory is freed after the final
+    // CTA barrier, which also orders the last TMEM reads).
+    bool last_entry = false;
     auto release = [&](uint32_t bar) {
+      if (last_entry) return;
       tc_fence_before();
       __syncwarp();
       if (lane == 0) {
@@ -770,6 +775,7 @@ __global__ void __launch_bounds__(kWsThreads, 1)
       int cm, tn;
       bool narrow;
       first.coords(p, idx, cm, tn, narrow);
+      last_entry = idx + p.nclusters >= p.tiles;
       const int row0 = (cm * p.cl + static_cast<int>(rank)) * BM + q * ROWS_W;   // first row of this warp
       const int width = narrow ? p.bn * NB / 2 : p.bn * NB;   // output columns of this tile
       const int col0 = tn * width;
