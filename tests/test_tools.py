@@ -1,0 +1,89 @@
+"""Host-side measurement tools, on the CPU: config lookup with modifiers (hopper_wgmma.ladder.lookup), the Nsight
+Compute report pipeline (hopper_wgmma.ncu_table, hopper_wgmma.report; the reference's scripts/ncu_table.py and
+scripts/report.py) and bench.py's choice of config per problem size."""
+from __future__ import annotations
+
+import json
+import sys
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def test_lookup_modifiers():
+  from hopper_wgmma.ladder import B200, LADDER, lookup
+  assert lookup("cluster_hilbert") is LADDER["cluster_hilbert"]
+  assert lookup("pair_wide") is B200["pair_wide"]
+  c = lookup("cta_n128@sk2")
+  assert c.split_k == 2 and c.BN == 128 and c.tma_store
+  assert lookup("cta_n64@skA").split_k == -1
+  c = lookup("cta_n64@reg@s4")
+  assert not c.tma_store and c.stages == 4 and c.BN == 64
+  with pytest.raises(KeyError):
+    lookup("cta_n64@bogus")
+  with pytest.raises(KeyError):
+    lookup("no_such_config")
+  with pytest.raises(ValueError):
+    lookup("tma_ring@sk2")   # a gated (non-persistent) config has no split-K
+
+
+CSV = """==PROF== Connected
+"ID","Process ID","Process Name","Host Name","Kernel Name","Context","Stream","Block Size","Grid Size","Device","CC","Section Name","Metric Name","Metric Unit","Metric Value"
+"0","1","python","h","void sm100::sm100_gemm_ws<128, 1, 1, 1, 0>(CUtensorMap_st, GemmParams)","1","7","(256, 1, 1)","(148, 1, 1)","0","10.0","Command line profiler metrics","gpu__time_duration.sum","usecond","95.50"
+"1","1","python","h","void sm100::sm100_gemm_ws<128, 1, 1, 1, 0>(CUtensorMap_st, GemmParams)","1","7","(256, 1, 1)","(148, 1, 1)","0","10.0","Command line profiler metrics","gpu__time_duration.sum","usecond","93.25"
+"2","1","python","h","nvjet_tst_256x256_64x4_2x2_2cta_v_bz_TNT","1","7","(384, 1, 1)","(148, 1, 1)","0","10.0","Command line profiler metrics","gpu__time_duration.sum","nsecond","96580"
+"""
+
+
+def test_ncu_table_best_and_launch_list():
+  from hopper_wgmma import ncu_table
+  best = ncu_table.best(CSV)
+  assert best["sm100::sm100_gemm_ws<128, 1, 1, 1, 0>"] == pytest.approx(93.25)
+  assert best["nvjet_tst_256x256_64x4_2x2_2cta_v_bz_TNT"] == pytest.approx(96.58)
+  rows = ncu_table.launch_list(CSV)
+  assert rows[0][0].startswith("sm100::") and rows[0][1] == 2
+  assert sum(r[3] for r in rows) == pytest.approx(1.0)
+  assert ncu_table.tflops(93.25, 4096, 4096, 4096) == pytest.approx(2 * 4096 ** 3 / 93.25e-6 / 1e12)
+
+
+def test_ncu_summary_table():
+  from hopper_wgmma import report
+  recs = [{"label": "cluster_hilbert", "shape": [4096, 4096, 4096], "us_best": 93.0, "tflops": 1478.0,
+           "cublas_us_best": 96.0, "cublas_tflops": 1431.0, "pct_cublas": 103.2},
+          {"label": "hilbert", "shape": [4096, 4096, 4096], "us_best": 99.0, "tflops": 1388.0,
+           "cublas_us_best": 96.0, "cublas_tflops": 1431.0, "pct_cublas": 97.0},
+          {"label": "cta_n128", "shape": [512, 512, 512], "us_best": 6.5, "tflops": 41.0,
+           "cublas_us_best": 4.3, "cublas_tflops": 62.0, "pct_cublas": 66.0}]
+  text = "\n".join("NCU " + json.dumps(r) for r in recs) + "\nERROR 8192x8192x8192: ncu exited 9: x\n"
+  md = report.ncu_summary([text], peak_tflops=1624.7)
+  lines = md.splitlines()
+  assert lines[2].startswith("| 512×512×512 | cta_n128 |")                      # smallest shape first
+  assert lines[3].startswith("| 4096×4096×4096 | cluster_hilbert | 93.0 | 1478 | 1431 | 103.2% | 91.0% |")
+  assert "**4096×4096×4096** — cluster_hilbert 103.2%, hilbert 97.0%" in md
+
+
+def test_bench_picks_wide_tiles_from_8192_squared_outputs():
+  sys.path.insert(0, str(ROOT))
+  import bench
+  name, cfg = bench.pick_cfg("best", 4096, 4096)
+  assert name == "best" and cfg.n_mma == 1 and cfg.cluster == 2 and cfg.hilbert
+  _, cfg = bench.pick_cfg("best", 8192, 8192)
+  assert cfg.n_mma == 2 and cfg.cluster == 2
+  _, cfg = bench.pick_cfg("best", 32768, 4096)           # one rank of the 8-GPU 32768^3 shard
+  assert cfg.n_mma == 2
+  name, cfg = bench.pick_cfg("cta_n128@sk2", 1024, 1024)
+  assert name == "cta_n128@sk2" and cfg.split_k == 2
+  with pytest.raises(SystemExit):
+    bench.pick_cfg("no_such_config", 4096, 4096)
+
+
+def test_bench_reads_traffic_lines_of_the_committed_profiles():
+  sys.path.insert(0, str(ROOT))
+  import bench
+  flops = 2.0 * 4096 ** 3
+  t = bench.profiled_traffic("sm100_gemm_ws_pair_tmast", "gemm4096", flops)
+  assert t is not None and 67_108_864 <= t <= 2 * 101_000_000      # at least the compulsory A + B
+  assert bench.profiled_traffic("sm100_gemm_ws_pair_tmast_x2", "gemm8192", 2.0 * 8192 ** 3) is not None
+  assert bench.profiled_traffic("no_such_kernel", "gemm4096", flops) is None
