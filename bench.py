@@ -189,15 +189,13 @@ def run_reference(args):
 # ------------------------------------------------------------------------------------------------------------------
 # our arm
 # ------------------------------------------------------------------------------------------------------------------
-def pick_cfg(name: str, m: int, n: int):
-  """``best`` = the fastest config of the ncu shape sweep for this size of per-rank GEMM: 256x256 CTA-pair tiles up to
-  about 6144^2 outputs, 256x512 pair tiles (two N = 256 MMAs per K step) from 8192^2 outputs up. Any other name is
-  looked up in the ladder tables (``hopper_wgmma.ladder.lookup``, modifiers such as ``@skA`` included)."""
-  from hopper_wgmma import WSCfg
-  from hopper_wgmma.ladder import lookup
-  if name == "best":
-    if m * n >= 8192 * 8192: return "best", WSCfg(tma_store=True, cluster=2, n_mma=2, hilbert=True)
-    return "best", WSCfg(tma_store=True, cluster=2, hilbert=True)
+def pick_cfg(name: str, m: int, n: int, k: int):
+  """``best`` = the fastest config of the ncu shape sweep for this size of per-rank GEMM
+  (``hopper_wgmma.ladder.best_config``: 256x256 CTA-pair tiles for the 4096^3 workload, 256x512 pair tiles from 8192^3
+  up). Any other name is looked up in the ladder tables (``hopper_wgmma.ladder.lookup``, modifiers such as ``@skA``
+  included)."""
+  from hopper_wgmma.ladder import best_config, lookup
+  if name == "best": return "best", best_config(m, n, k)
   try:
     return name, lookup(name)
   except (KeyError, ValueError) as exc:
@@ -224,7 +222,7 @@ def run_ours(args):
     if world > 1: dist.barrier()
 
   M, n, K, N_total, scaling = shapes(args.workload, world)
-  cfg_name, cfg = pick_cfg(args.cfg, M, n)
+  cfg_name, cfg = pick_cfg(args.cfg, M, n, K)
   flops_rank = 2.0 * M * n * K
 
   # inputs resident in HBM: A replicated (same seed everywhere), this rank's K-major B shard, this rank's C shard

@@ -64,19 +64,31 @@ def test_ncu_summary_table():
   assert "**4096×4096×4096** — cluster_hilbert 103.2%, hilbert 97.0%" in md
 
 
-def test_bench_picks_wide_tiles_from_8192_squared_outputs():
+def test_best_config_by_size():
+  from hopper_wgmma.ladder import B200, LADDER, best_config
+  assert best_config(8192, 8192, 8192) is B200["pair_wide_hilbert"]
+  assert best_config(32768, 4096, 32768) is B200["pair_wide_hilbert"]     # one rank of the 8-GPU 32768^3 shard
+  assert best_config(4096, 4096, 4096) is LADDER["cluster_hilbert"]
+  assert best_config(8192, 8192, 2048) is LADDER["cluster_hilbert"]       # short K: 256x256 pairs (104 % of cuBLAS)
+  assert best_config(2048, 2048, 16384) is LADDER["cluster_hilbert"]
+  assert best_config(2048, 2048, 2048) is LADDER["hilbert"]
+  small = best_config(1024, 1024, 8192)
+  assert small.BN == 128 and small.cluster == 1 and small.split_k == -1
+
+
+def test_bench_picks_the_best_config_for_the_rank_size():
   sys.path.insert(0, str(ROOT))
   import bench
-  name, cfg = bench.pick_cfg("best", 4096, 4096)
+  name, cfg = bench.pick_cfg("best", 4096, 4096, 4096)
   assert name == "best" and cfg.n_mma == 1 and cfg.cluster == 2 and cfg.hilbert
-  _, cfg = bench.pick_cfg("best", 8192, 8192)
+  _, cfg = bench.pick_cfg("best", 8192, 8192, 8192)
   assert cfg.n_mma == 2 and cfg.cluster == 2
-  _, cfg = bench.pick_cfg("best", 32768, 4096)           # one rank of the 8-GPU 32768^3 shard
+  _, cfg = bench.pick_cfg("best", 32768, 4096, 32768)
   assert cfg.n_mma == 2
-  name, cfg = bench.pick_cfg("cta_n128@sk2", 1024, 1024)
+  name, cfg = bench.pick_cfg("cta_n128@sk2", 1024, 1024, 1024)
   assert name == "cta_n128@sk2" and cfg.split_k == 2
   with pytest.raises(SystemExit):
-    bench.pick_cfg("no_such_config", 4096, 4096)
+    bench.pick_cfg("no_such_config", 4096, 4096, 4096)
 
 
 def test_bench_reads_traffic_lines_of_the_committed_profiles():
