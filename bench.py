@@ -300,8 +300,8 @@ def run_ours(args):
   cub_tflops = flops_rank * world / (cub_med * 1e-3) / 1e12
 
   # End to end through the public API, as a caller streaming batches would run it: every step copies its A and B
-  # from pinned host memory, runs the reference-facing operator build_gemm_ws(...)(A, B, C)() (K-major copy of B,
-  # plan, launch) and copies C back to pinned host memory. Steps rotate over three streams and buffer sets (two when
+  # from pinned host memory, runs the reference-facing operator build_gemm_ws(...)(A, B, C)() (plan and launch; B is
+  # read as given for CTA-pair tiles, copied K-major first otherwise) and copies C back to pinned host memory. Steps rotate over three streams and buffer sets (two when
   # a set would exceed 1 GiB), so one step's host-to-device copies overlap earlier steps' GEMMs and device-to-host
   # copies without queueing behind them on a shared stream.
   e2e = None
@@ -345,8 +345,9 @@ def run_ours(args):
     if world > 1: e2e_ms = shard.max_over_ranks(e2e_ms, device=dev)
     e2e = {"value": round(flops_rank * world / (e2e_ms / e2e_steps * 1e-3) / 1e12, 3), "unit": "TFLOPS",
            "h2d_bytes_per_step": 2 * (M * K + K * n), "d2h_bytes_per_step": 2 * M * n,
-           "path": "pinned host A,B -> build_gemm_ws(...)(A, B, C)() (K-major copy of B, plan, launch) -> pinned host C; "
-                   f"{nsets} streams and buffer sets, steps overlapped",
+           "path": "pinned host A,B -> build_gemm_ws(...)(A, B, C)() ("
+                   f"{'B read N-major as given' if cfg.reads_b_directly else 'K-major copy of B'}, plan, launch) -> "
+                   f"pinned host C; {nsets} streams and buffer sets, steps overlapped",
            "steps": e2e_steps, "ms_per_step": round(e2e_ms / e2e_steps, 4)}
 
   # Optional NCCL all-gather of the C shards over NVLink (A replicated, B and C column-sharded): timed separately,

@@ -2,8 +2,9 @@
  * sm100_gemm.h — C ABI of the B200 (sm_100a) bf16 GEMM that stands in for the Hopper wgmma GEMM of
  * narain1/tinygrad-hopper-wgmma. Plain pointers, sizes and status codes; no framework types.
  *
- *   C[M,N] (bf16) = A[M,K] (bf16, row-major) x B[K,N], with B supplied K-major as BT[N,K] (row-major), fp32
- *   accumulation, bf16 output rounded to nearest even. M, N and K are multiples of the tile.
+ *   C[M,N] (bf16) = A[M,K] (bf16, row-major) x B[K,N], with B supplied K-major as BT[N,K] (row-major) or, with
+ *   bg_cfg.b_nmajor = 1, as B[K,N] itself; fp32 accumulation, bf16 output rounded to nearest even. M, N and K are
+ *   multiples of the tile unless bg_cfg.ragged is set.
  *
  * Status codes: 0 = ok; negative = the arguments break the operator's contract (the Python layer raises
  * ValueError, as the reference does for config and shape errors); positive = a CUDA / driver error or a device-side
@@ -74,6 +75,12 @@ enum {
  *   no_k_serpentine 0 (default): a persistent cluster walks K forwards on its even-numbered tiles and backwards on
  *               its odd-numbered ones, so each wave starts on the K-slabs the previous wave left in L2 (fewer DRAM
  *               reads); 1: always forwards (the fp32 accumulation order of every tile then runs along K)
+ *   b_nmajor    0 (default): the B operand is BT[N,K] (K-major, row pitch ldb >= K), as the reference's kernel takes
+ *               it after its transpose (gemm.py:382). 1 (warp-specialized kernel): the B operand is B[K,N] itself
+ *               (N-major, row pitch ldb >= N; a column block of a wider B is allowed), read through MN-major
+ *               tcgen05 descriptors, so the caller makes no transposed copy. Needs each CTA's share of a tile's
+ *               columns (BN, or BN / 2 in a CTA pair) to be a multiple of 64; half-width tail tiles are used only
+ *               when their share is too.
  */
 typedef struct bg_cfg {
   int32_t kind;
@@ -95,6 +102,7 @@ typedef struct bg_cfg {
   int32_t ragged;
   int32_t split_k;
   int32_t no_k_serpentine;
+  int32_t b_nmajor;
 } bg_cfg;
 
 /* What a plan resolved to (for reports and tests). */
@@ -135,7 +143,8 @@ int32_t bg_device_info(int32_t device, int32_t* sm_count, int32_t* smem_optin, i
  * the tensor maps (tensor_map.py:13-33), builds the tile table (gemm.py:200-240) in device memory, allocates the
  * error word and sets the kernel's launch attributes (runtime.py:20-98).
  *   A   device pointer, M rows, row pitch lda elements (>= K)
- *   BT  device pointer, N rows, row pitch ldb elements (>= K)
+ *   BT  device pointer, N rows, row pitch ldb elements (>= K); with cfg->b_nmajor = 1 it is B[K,N]: K rows, row
+ *       pitch ldb elements (>= N), and a column block of a wider B is allowed
  *   C   device pointer, M rows, row pitch ldc elements (>= N); a column shard of a wider C is allowed
  * All pointers 16-byte aligned, all pitches multiples of 8 elements. The plan keeps the raw pointers: the caller keeps
  * the buffers alive for the plan's life (as the reference keeps A and BT alive in launch, gemm.py:394).

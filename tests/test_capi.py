@@ -49,6 +49,10 @@ def _cfg(**kw):
   ({"split_k": 2, "kind": 1}, (512, 512, 512), "split_k needs the persistent kernel"),
   ({"split_k": 9}, (512, 512, 512), "exceeds the 8 k-blocks"),
   ({"split_k": 2, "BN": 48}, (512, 480, 512), "multiple of 32 columns"),
+  ({"b_nmajor": 2}, (512, 512, 512), "b_nmajor must be 0 or 1"),
+  ({"b_nmajor": 1, "kind": 1}, (512, 512, 512), "b_nmajor needs the warp-specialized kernel"),
+  ({"b_nmajor": 1, "BN": 96}, (512, 576, 512), "b_nmajor needs BN a multiple of 64"),
+  ({"b_nmajor": 1, "BN": 64, "cluster": 2}, (512, 512, 512), "b_nmajor needs BN / 2 a multiple of 64"),
 ])
 def test_contract_violations_are_negative_status(kw, shape, msg):
   st, err = _create(_cfg(**kw), *shape)
@@ -63,6 +67,9 @@ def test_pointer_and_pitch_checks():
   st, err = _create(_cfg(), 512, 512, 512, lda=256)
   assert st < 0 and "row pitches" in err
   st, err = _create(_cfg(), 512, 512, 512, ldc=516)
+  assert st < 0 and "row pitches" in err
+  # N-major B: its pitch covers N, not K
+  st, err = _create(_cfg(b_nmajor=1), 512, 1024, 256, ldb=512)
   assert st < 0 and "row pitches" in err
 
 

@@ -152,6 +152,68 @@ def test_b200_cases(idx, cuda_dev):
   assert worst <= TOL, f"{name} {M}x{N}x{K}: relative_error={worst:.5f} ({launch.info()['kernel']})"
 
 
+# ------------------------------------------------------------------------------------------------------------------
+# B operand layouts: B[K,N] read N-major as given (the default where the tile allows it) and the reference's K-major
+# copy BT[N,K] (gemm.py:382), on the same configs
+# ------------------------------------------------------------------------------------------------------------------
+def _layout_cases():
+  from hopper_wgmma import WSCfg
+  return [
+    ("cluster_hilbert", WSCfg(tma_store=True, hilbert=True, cluster=2), (512, 512, 512)),
+    ("cta_bn256_regstore", WSCfg(), (512, 512, 320)),                          # 4 boxes of 64 columns per stage
+    ("cta_bn192_no_tail", WSCfg(BN=192, tma_store=True, split_tail=False), (256, 768, 256)),
+    ("m64_bn128", WSCfg(consumers=1, BN=128, tma_store=True, hilbert=True), (320, 384, 192)),
+    ("pair_wide", WSCfg(tma_store=True, cluster=2, n_mma=2), (512, 1024, 256)),
+    ("wide_split_abc", WSCfg(n_mma=2, cluster=2, tma_store=True, split_tail=False), (512, 1024, 1024)),
+    ("tail_split_pair", WSCfg(tma_store=True, cluster=2, hilbert=True, num_sm=18), (1024, 1792, 128)),
+    ("tail_split_cta", WSCfg(BN=128, tma_store=True, num_sm=6), (512, 640, 192)),
+    ("tail_split_wide_pair", WSCfg(n_mma=2, cluster=2, tma_store=True, num_sm=10), (1024, 1536, 128)),
+    ("ragged_pair", WSCfg(tma_store=True, hilbert=True, cluster=2, ragged=True), (1000, 1000, 520)),
+    ("ragged_cta_reg", WSCfg(BN=128, ragged=True, num_sm=9), (333, 712, 136)),
+    ("split_k4", WSCfg(BN=128, tma_store=True, split_k=4), (256, 256, 4096)),
+    ("split_k2_wide_pair", WSCfg(n_mma=2, cluster=2, tma_store=True, split_k=2), (256, 1024, 2048)),
+    ("serpentine_waves", WSCfg(n_mma=2, cluster=2, tma_store=True, num_sm=10), (1024, 2048, 640)),
+  ]
+
+
+@pytest.mark.parametrize("layout", ["N", "K"])
+@pytest.mark.parametrize("idx", range(14))
+def test_b_operand_layouts(idx, layout, cuda_dev):
+  import dataclasses
+  from hopper_wgmma import build_gemm_ws
+  name, cfg, (M, N, K) = _layout_cases()[idx]
+  cfg = dataclasses.replace(cfg, b_nmajor=layout == "N")
+  assert cfg.reads_b_directly == (layout == "N"), name
+  worst, launch = run_case(lambda: build_gemm_ws(N, cfg, M, K, wait_budget_ns=BUDGET_NS), M, N, K, cuda_dev)
+  kernel = launch.info()["kernel"]
+  assert kernel.endswith(f"b={layout}"), kernel
+  assert worst <= TOL, f"{name} b={layout} {M}x{N}x{K}: relative_error={worst:.5f} ({kernel})"
+
+
+def test_n_major_b_column_views(cuda_dev):
+  """plan_gemm_b on a column block of B and of C (both row pitches > N): a rank's shard needs no copy of B."""
+  torch = _torch()
+  from hopper_wgmma import WSCfg
+  from hopper_wgmma.gemm import plan_gemm_b
+  from oracle import gemm_ref
+  M, N, K, W = 512, 2048, 384, 4
+  a_bits, b_bits = inputs(M, N, K, seed=5)
+  A, B = to_dev(a_bits, cuda_dev), to_dev(b_bits, cuda_dev)
+  C = torch.full((M, N), 7.0, dtype=torch.bfloat16, device=cuda_dev)
+  ref = gemm_ref.gemm_f32(a_bits, b_bits)
+  n = N // W
+  for r, cfg in ((1, WSCfg(tma_store=True, cluster=2, hilbert=True)), (3, WSCfg(BN=128, consumers=1))):
+    launch = plan_gemm_b(A, B[:, r * n:(r + 1) * n], C[:, r * n:(r + 1) * n], cfg, wait_budget_ns=BUDGET_NS)
+    launch()
+    launch.check()
+    assert launch.info()["kernel"].endswith("b=N")
+  out = to_bits(C)
+  for r in (1, 3):
+    assert gemm_ref.rel_err(out[:, r * n:(r + 1) * n], ref[:, r * n:(r + 1) * n]) <= TOL
+  rest = np.concatenate([out[:, :n], out[:, 2 * n:3 * n]], axis=1)
+  assert (gemm_ref.bf16_bits_to_f32(rest) == 7.0).all()
+
+
 def test_matches_cublas_bitwise_or_close(cuda_dev):
   """Against torch.matmul (cuBLAS) on the same bf16 inputs: the reference printed rel=0.00000 for every CHECK
   (scripts/ncu_workload.py:60-64). Both accumulate in fp32 and round to bf16, so most elements are bitwise equal;

@@ -40,14 +40,14 @@ def test_library_reports_missing_device_as_runtime_error_not_crash():
 
 
 def test_cfg_struct_layout_matches_header():
-  """The ctypes mirror of bg_cfg has the header's fields in order (12 int32, int64, 6 int32)."""
+  """The ctypes mirror of bg_cfg has the header's fields in order (12 int32, int64, 7 int32, padded to 8 bytes)."""
   import ctypes
   from hopper_wgmma import _capi
   text = (ROOT / "include" / "sm100_gemm.h").read_text()
   body = text[text.index("typedef struct bg_cfg {"):text.index("} bg_cfg;")]
   fields = re.findall(r"int(?:32|64)_t\s+(\w+);", body)
   assert [f for f, _ in _capi.BgCfg._fields_] == fields
-  assert ctypes.sizeof(_capi.BgCfg) == 12 * 4 + 8 + 6 * 4
+  assert ctypes.sizeof(_capi.BgCfg) == 12 * 4 + 8 + 7 * 4 + 4
 
 
 # ----------------------------------------------------------------------------------------------------------------
@@ -102,6 +102,31 @@ def test_b200_knobs_validate():
     WSCfg(BN=48, split_k=2)
   assert WSCfg(split_k=4).name.endswith("_sk4") and WSCfg(split_k=4).to_c().split_k == 4
   assert WSCfg(split_k=-1).name.endswith("_skA") and WSCfg(split_k=-1).to_c().split_k == -1
+
+
+def test_which_configs_read_b_directly():
+  """build_gemm_ws hands B[K,N] to the kernel uncopied when every CTA's share of a tile's columns, and of a
+  half-width tail tile's, is whole 64-column boxes; by default only CTA pairs do (single-CTA tiles measured slower
+  with N-major B). Otherwise it makes the reference's K-major copy."""
+  import dataclasses
+  from hopper_wgmma import WSCfg
+  from hopper_wgmma.ladder import B200, LADDER
+  for name in ("cluster", "cluster_hilbert"):
+    assert LADDER[name].reads_b_directly, name                 # 256x256 pair tiles, 128 columns per CTA
+  assert B200["pair_wide_hilbert"].reads_b_directly             # two N blocks of 128 columns per CTA
+  for name in ("role_split", "tma_store", "hilbert"):
+    assert not LADDER[name].reads_b_directly, name             # single-CTA tiles copy by default ...
+    assert dataclasses.replace(LADDER[name], b_nmajor=True).reads_b_directly, name   # ... and can read directly
+  forced = {k: dataclasses.replace(v, b_nmajor=True) for k, v in B200.items()}
+  assert forced["cta_n128"].reads_b_directly and forced["m64_n128"].reads_b_directly
+  assert not forced["cta_n64"].reads_b_directly                # its half-width tail tiles are 32 columns
+  assert WSCfg(BN=64, tma_store=True, split_tail=False, b_nmajor=True).reads_b_directly
+  assert not forced["pair_n128"].reads_b_directly              # 64 columns per CTA, 32 in a tail tile
+  assert not forced["pair_n192"].reads_b_directly              # 96 columns per CTA
+  assert not WSCfg(cluster=2, b_nmajor=False).reads_b_directly
+  assert WSCfg(b_nmajor=False).name.endswith("_bT") and WSCfg(b_nmajor=True).name.endswith("_bN")
+  assert not WSCfg().name.endswith(("_bT", "_bN"))
+  assert WSCfg().to_c().b_nmajor == 0 and WSCfg().to_c(b_nmajor=True).b_nmajor == 1
 
 
 # ----------------------------------------------------------------------------------------------------------------

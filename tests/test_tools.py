@@ -21,6 +21,9 @@ def test_lookup_modifiers():
   assert lookup("cta_n64@skA").split_k == -1
   c = lookup("cta_n64@reg@s4")
   assert not c.tma_store and c.stages == 4 and c.BN == 64
+  c = lookup("cluster_hilbert@bT")
+  assert c.b_nmajor is False and c.cluster == 2 and LADDER["cluster_hilbert"].b_nmajor is None
+  assert lookup("cta_n128@bN").b_nmajor is True
   with pytest.raises(KeyError):
     lookup("cta_n64@bogus")
   with pytest.raises(KeyError):

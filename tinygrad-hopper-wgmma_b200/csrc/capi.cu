@@ -162,7 +162,8 @@ uint32_t pow2_cols(int n) {
 }
 
 // tcgen05 instruction descriptor, kind::f16: D f32 (bits 4-5 = 1), A bf16 (bits 7-9 = 1), B bf16 (bits 10-12 = 1),
-// both K-major (bits 15, 16 = 0), N >> 3 in bits 17-22, M >> 4 in bits 24-28.
+// both K-major (bits 15, 16 = 0), N >> 3 in bits 17-22, M >> 4 in bits 24-28. Bit 16 set = B is MN-major.
+constexpr uint32_t kIdescBMajorMN = 1u << 16;
 uint32_t make_idesc(int m, int n) {
   return (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(n >> 3) << 17) |
          (static_cast<uint32_t>(m >> 4) << 24);
@@ -383,6 +384,9 @@ int32_t setup_plan(const bg_cfg& c, int64_t M, int64_t N, int64_t K, const void*
   const bool sk_auto = c.split_k == -1;
   int sk = c.split_k <= 1 ? 1 : c.split_k;
   if (sk > 1 && c.kind != BG_KIND_WS) return fail(-1, "split_k needs the persistent kernel");
+  const bool nmajor = c.b_nmajor != 0;
+  if (c.b_nmajor != 0 && c.b_nmajor != 1) return fail(-1, "b_nmajor must be 0 or 1");
+  if (nmajor && c.kind != BG_KIND_WS) return fail(-1, "b_nmajor needs the warp-specialized kernel");
 
   const int bm = 64 * std::max(c.consumers, 1);
   const int cl = c.cluster;
@@ -392,6 +396,9 @@ int32_t setup_plan(const bg_cfg& c, int64_t M, int64_t N, int64_t K, const void*
   if (nblk < 1 || nblk > 2 || (nblk > 1 && c.kind != BG_KIND_WS)) return fail(-1, "n_mma must be 1 or 2 (persistent kernel)");
   const int width = bn * nblk;   // output columns per tile
   const int bn_local = paired ? bn / 2 : bn;
+  // N-major B arrives in 64-column boxes: every CTA's share of an N block must be whole boxes
+  if (nmajor && bn_local % 64)
+    return fail(-1, "b_nmajor needs %s a multiple of 64 columns (got %d)", paired ? "BN / 2" : "BN", bn_local);
 
   // ---- shape contract (gemm.py:300-311)
   if (M <= 0 || N <= 0 || K <= 0) return fail(-1, "M, N and K must be positive");
@@ -417,7 +424,7 @@ int32_t setup_plan(const bg_cfg& c, int64_t M, int64_t N, int64_t K, const void*
   if (A == nullptr || BT == nullptr || C == nullptr) return fail(-1, "null operand pointer");
   if ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(BT) | reinterpret_cast<uintptr_t>(C)) & 15)
     return fail(-1, "operand pointers must be 16-byte aligned");
-  if (lda < K || ldb < K || ldc < N || lda % 8 || ldb % 8 || ldc % 8)
+  if (lda < K || ldb < (nmajor ? N : K) || ldc < N || lda % 8 || ldb % 8 || ldc % 8)
     return fail(-1, "row pitches must cover the row and be multiples of 8 elements (lda=%lld ldb=%lld ldc=%lld)",
                 (long long)lda, (long long)ldb, (long long)ldc);
 
@@ -539,7 +546,8 @@ int32_t setup_plan(const bg_cfg& c, int64_t M, int64_t N, int64_t K, const void*
   // dealt table) is split into half-width tiles when twice its size still fits in one wave, so that the tail takes
   // about half a tile's time instead of a whole one. Half width = one N block when nblk == 2, MMA N = BN/2 otherwise.
   const int half = nblk == 2 ? bn : bn / 2;
-  const bool narrow_ok = nblk == 2 || (half % 16 == 0 && (!c.tma_store || half % 64 == 0));
+  const bool narrow_ok =
+      nblk == 2 || (half % 16 == 0 && (!c.tma_store || half % 64 == 0) && (!nmajor || (half / cl) % 64 == 0));
   int64_t n_entries = tiles;
   if (c.kind == BG_KIND_WS && !c.no_tail_split && sk == 1 && narrow_ok && !sched.empty()) {
     const int64_t full = (tiles / nclusters) * nclusters;
@@ -576,13 +584,20 @@ int32_t setup_plan(const bg_cfg& c, int64_t M, int64_t N, int64_t K, const void*
   nclusters = std::min<int64_t>(nclusters, n_entries);
   p->grid = static_cast<int>(nclusters * (c.kind == BG_KIND_RING ? 1 : cl));
 
-  // ---- tensor maps: A[M,K] box (64, BM); BT[N,K] box (64, bn_local); C[M,N] box (64, BM/4) per epilogue warp
+  // ---- tensor maps: A[M,K] box (64, BM); BT[N,K] box (64, bn_local), or B[K,N] box (64, 64) when N-major;
+  // C[M,N] box (64, BM/4) per epilogue warp
   if ((st = encode_2d(&p->tmA, A, K, M, lda, 64, bm, "A"))) return st;
-  if ((st = encode_2d(&p->tmB, BT, K, N, ldb, 64, bn_local, "BT"))) return st;
-  if (nblk == 1 && p->narrow_tiles > 0) {
-    if ((st = encode_2d(&p->tmBn, BT, K, N, ldb, 64, bn_local / 2, "BT half tiles"))) return st;
-  } else {
+  if (nmajor) {
+    // 64-column x 64-row boxes (one 128-byte swizzle row of N per K row) serve full and half-width tiles alike
+    if ((st = encode_2d(&p->tmB, BT, N, K, ldb, 64, 64, "B (N-major)"))) return st;
     p->tmBn = p->tmB;
+  } else {
+    if ((st = encode_2d(&p->tmB, BT, K, N, ldb, 64, bn_local, "BT"))) return st;
+    if (nblk == 1 && p->narrow_tiles > 0) {
+      if ((st = encode_2d(&p->tmBn, BT, K, N, ldb, 64, bn_local / 2, "BT half tiles"))) return st;
+    } else {
+      p->tmBn = p->tmB;
+    }
   }
   if (p->tma_store) {
     if ((st = encode_2d(&p->tmC, C, N, M, ldc, 64, bm / 4, "C"))) return st;
@@ -603,10 +618,11 @@ int32_t setup_plan(const bg_cfg& c, int64_t M, int64_t N, int64_t K, const void*
   kp.acc_bufs = acc_bufs;
   kp.acc_stride = width;
   kp.tmem_cols = pow2_cols(acc_bufs * width);
-  kp.idesc = make_idesc(paired ? 2 * bm : bm, bn);
+  const uint32_t b_mn = nmajor ? kIdescBMajorMN : 0u;
+  kp.idesc = make_idesc(paired ? 2 * bm : bm, bn) | b_mn;
   kp.tx_bytes = (a_stage + b_stage) * (paired ? 2u : 1u);
   kp.tx_narrow = (a_stage + (nblk == 2 ? b_block : b_block / 2)) * (paired ? 2u : 1u);
-  kp.idesc_narrow = make_idesc(paired ? 2 * bm : bm, nblk == 2 ? bn : bn / 2);
+  kp.idesc_narrow = make_idesc(paired ? 2 * bm : bm, nblk == 2 ? bn : bn / 2) | b_mn;
   kp.a_stage_bytes = a_stage;
   kp.b_block_bytes = b_block;
   kp.b_stage_bytes = b_stage;
@@ -623,6 +639,7 @@ int32_t setup_plan(const bg_cfg& c, int64_t M, int64_t N, int64_t K, const void*
   kp.tickets = nullptr;
   kp.sk_scatter = sk_scatter ? 1 : 0;
   kp.k_serpentine = c.no_k_serpentine ? 0 : 1;
+  kp.b_nmajor = nmajor ? 1 : 0;
   // A cooperative launch guarantees that every CTA is resident at once. It cannot be combined with cluster
   // dimensions here (such a launch fails under Nsight Compute), so CTA pairs rely on the persistent grid being
   // capped at what the GPU co-schedules, with the bounded wait reporting an error if other work holds SMs.
@@ -633,10 +650,10 @@ int32_t setup_plan(const bg_cfg& c, int64_t M, int64_t N, int64_t K, const void*
   // the first wave of the tile table also travels in the kernel parameters (see FirstTile in the kernel)
   for (size_t i = 0; i < sched.size() && i < static_cast<size_t>(sm100::kFirstWave); ++i) kp.first_wave[i] = sched[i];
 
-  snprintf(p->name, sizeof(p->name), "%s<BM=%d,%s,%s> BN=%dx%d stages=%d acc=%d tail=%d splitk=%d",
+  snprintf(p->name, sizeof(p->name), "%s<BM=%d,%s,%s> BN=%dx%d stages=%d acc=%d tail=%d splitk=%d b=%s",
            c.kind == BG_KIND_RING ? "sm100_gemm_ring" : "sm100_gemm_ws", bm,
            paired ? "pair" : (cl == 2 ? "cluster2" : "cta"), p->tma_store ? "tma_store" : "reg_store", bn, nblk,
-           stages, acc_bufs, p->narrow_tiles, sk);
+           stages, acc_bufs, p->narrow_tiles, sk, nmajor ? "N" : "K");
   return 0;
 }
 

@@ -1,5 +1,6 @@
-// bf16 GEMM kernels for sm_100a: C[M,N] = A[M,K] * B[K,N], operands K-major (A row-major, B given as BT[N,K]),
-// fp32 accumulation in tensor memory, bf16 output. Shapes are tile multiples unless the host asks for ragged edges
+// bf16 GEMM kernels for sm_100a: C[M,N] = A[M,K] * B[K,N], A K-major (row-major), B either K-major (given as
+// BT[N,K]) or, for sm100_gemm_ws, N-major (B[K,N] as it is, read through MN-major tcgen05 descriptors), fp32
+// accumulation in tensor memory, bf16 output. Shapes are tile multiples unless the host asks for ragged edges
 // (TMA zero-fills loads past the operands; stores are clipped or masked).
 //
 //   sm100_gemm_ws    warp-specialized tcgen05 GEMM. Used for the reference's persistent ladder rungs
@@ -41,7 +42,8 @@ constexpr int kBK = 64;           // K per pipeline stage: one 128-byte swizzle 
 constexpr int kWsThreads = 256;   // warps 0-3 producer / MMA / idle, warps 4-7 epilogue
 constexpr int kRingThreads = 128;
 constexpr int kFirstWave = 160;   // first-wave tile entries passed in the kernel parameters (>= clusters on a B200)
-constexpr int kSkSlots = 8;       // split-K reduce: 4 KB shared-memory slots per epilogue warp (in the idle ring)
+constexpr int kSkSlots = 8;
+constexpr uint32_t kNmajorChunk = 64 * 128;   // one N-major B box in shared memory: 64 K rows x 64 columns of bf16       // split-K reduce: 4 KB shared-memory slots per epilogue warp (in the idle ring)
 
 // Error word layout: role in bits 24-31, the role's job or tile counter (saturated) in bits 0-23.
 enum : uint32_t {
@@ -92,6 +94,7 @@ struct GemmParams {
                            // partial sums are written; zero between launches
   int sk_scatter;          // split-K with one entry per cluster, launched cooperatively: the reduce is shared out
   int k_serpentine;        // a cluster walks K backwards on its odd-numbered tiles (1) or always forwards (0)
+  int b_nmajor;            // B is given as B[K,N] row-major (1; tmB/tmBn map it with 64 x 64 boxes) or as BT[N,K] (0)
   int32_t first_wave[kFirstWave];  // sched[0 .. min(tiles, kFirstWave)) again, delivered with the launch
 };
 
@@ -297,19 +300,38 @@ __global__ void __launch_bounds__(kWsThreads, 1)
           const uint32_t fb = full0 + 8u * stage;
           const uint32_t a_dst = sA + stage * p.a_stage_bytes;
           const uint32_t b_dst = sB + stage * p.b_stage_bytes;
+          // N-major B: this CTA's columns of an N block arrive as 64-column x 64-row boxes, 8 KB apart (the MMA's
+          // leading byte offset); K-major B: one box of bn_local (or half that) rows of BT
+          const int chunks = p.b_nmajor ? (bsub / CG) >> 6 : 0;
           if (PAIRED) {
             const uint32_t fb_leader = mapa_shared(fb, 0);
             if (leader) mbar_arrive_expect_tx(fb, tx);
             tma_load_2d_pair(a_dst, &tmA, fb_leader, kc * kBK, row_a);
 #pragma unroll
-            for (int nb = 0; nb < NB; ++nb)
-              if (nb < nblk) tma_load_2d_pair(b_dst + nb * p.b_block_bytes, mapB, fb_leader, kc * kBK, row_b + nb * bsub);
+            for (int nb = 0; nb < NB; ++nb) {
+              if (nb >= nblk) continue;
+              if (p.b_nmajor) {
+                for (int j = 0; j < chunks; ++j)
+                  tma_load_2d_pair(b_dst + nb * p.b_block_bytes + j * kNmajorChunk, mapB, fb_leader,
+                                   row_b + nb * bsub + 64 * j, kc * kBK);
+              } else {
+                tma_load_2d_pair(b_dst + nb * p.b_block_bytes, mapB, fb_leader, kc * kBK, row_b + nb * bsub);
+              }
+            }
           } else {
             mbar_arrive_expect_tx(fb, tx);
             tma_load_2d(a_dst, &tmA, fb, kc * kBK, row_a);
 #pragma unroll
-            for (int nb = 0; nb < NB; ++nb)
-              if (nb < nblk) tma_load_2d(b_dst + nb * p.b_block_bytes, mapB, fb, kc * kBK, row_b + nb * bsub);
+            for (int nb = 0; nb < NB; ++nb) {
+              if (nb >= nblk) continue;
+              if (p.b_nmajor) {
+                for (int j = 0; j < chunks; ++j)
+                  tma_load_2d(b_dst + nb * p.b_block_bytes + j * kNmajorChunk, mapB, fb, row_b + nb * bsub + 64 * j,
+                              kc * kBK);
+              } else {
+                tma_load_2d(b_dst + nb * p.b_block_bytes, mapB, fb, kc * kBK, row_b + nb * bsub);
+              }
+            }
           }
         }
         __syncwarp();
@@ -348,11 +370,15 @@ __global__ void __launch_bounds__(kWsThreads, 1)
           ph ^= 1u;
         }
       };
+      // B's K16 step in descriptor address units: +32 bytes inside a K-major swizzle row, or +16 rows of 128 bytes
+      // (2048 bytes) for N-major B; the N-major descriptor's leading byte offset is the 8 KB between 64-column boxes
+      const uint32_t b_kstep = p.b_nmajor ? 128u : 2u;
+      const uint32_t b_lbo = p.b_nmajor ? (kNmajorChunk >> 4) : 1u;
       auto issue = [&](uint32_t st, int kb, int nb_lo, int nb_hi, uint32_t d, uint32_t idesc) {
         if (elect_one()) {
           const uint64_t ad = smem_desc_sw128(sA + st * p.a_stage_bytes);
-          const uint64_t bd = smem_desc_sw128(sB + st * p.b_stage_bytes);
-          // +32 bytes along K inside the swizzle row = +2 in the descriptor's address field; N block nb reads the
+          const uint64_t bd = smem_desc_sw128(sB + st * p.b_stage_bytes, b_lbo);
+          // A: +32 bytes along K inside the swizzle row = +2 in the descriptor's address field; N block nb reads the
           // nb-th B sub-tile and accumulates into TMEM columns [nb * bn, (nb + 1) * bn)
 #pragma unroll
           for (int k = 0; k < kBK / 16; ++k)
@@ -360,7 +386,7 @@ __global__ void __launch_bounds__(kWsThreads, 1)
             for (int nb = 0; nb < NB; ++nb)
               if (nb >= nb_lo && nb < nb_hi)
                 mma_bf16<CG>(d + static_cast<uint32_t>(nb * p.bn), ad + 2u * k,
-                             bd + static_cast<uint64_t>((nb * p.b_block_bytes) >> 4) + 2u * k, idesc,
+                             bd + static_cast<uint64_t>((nb * p.b_block_bytes) >> 4) + b_kstep * k, idesc,
                              (kb | k) != 0 ? 1u : 0u);
         }
         __syncwarp();

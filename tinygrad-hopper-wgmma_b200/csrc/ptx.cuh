@@ -233,15 +233,17 @@ __device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
-// Shared-memory matrix descriptor for a K-major bf16 tile written by TMA with 128-byte swizzle: rows of 128 bytes
-// (64 bf16 along K), 8-row swizzle atoms of 1024 bytes stacked along M/N. Fields (tcgen05 descriptor format):
-// start address >> 4 in bits 0-13, leading byte offset >> 4 in bits 16-29 (unused for swizzled K-major, set to 1),
-// stride byte offset >> 4 in bits 32-45 (1024 bytes between 8-row groups), version 1 in bits 46-47, base offset 0,
-// swizzle mode 2 (128B) in bits 61-63. The tile must start on a 1024-byte boundary.
-__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t smem_addr) {
+// Shared-memory matrix descriptor for a bf16 tile written by TMA with 128-byte swizzle: rows of 128 bytes, 8-row
+// swizzle atoms of 1024 bytes. Fields (tcgen05 descriptor format): start address >> 4 in bits 0-13, leading byte
+// offset >> 4 in bits 16-29, stride byte offset >> 4 in bits 32-45 (1024 bytes between 8-row groups), version 1 in
+// bits 46-47, base offset 0, swizzle mode 2 (128B) in bits 61-63. The tile must start on a 1024-byte boundary.
+//   K-major (rows run along M/N, 64 bf16 of K per row): the leading byte offset is unused (lbo16 = 1).
+//   MN-major (rows run along K, 64 bf16 of M/N per row): 8-row groups step along K by the stride byte offset, and
+//   64-column atoms step along M/N by the leading byte offset (lbo16 = that distance >> 4).
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t smem_addr, uint32_t lbo16 = 1u) {
   uint64_t d = 0;
   d |= static_cast<uint64_t>((smem_addr >> 4) & 0x3FFFu);
-  d |= static_cast<uint64_t>(1u) << 16;
+  d |= static_cast<uint64_t>(lbo16 & 0x3FFFu) << 16;
   d |= static_cast<uint64_t>(1024u >> 4) << 32;
   d |= static_cast<uint64_t>(1u) << 46;
   d |= static_cast<uint64_t>(2u) << 61;

@@ -147,6 +147,9 @@ class WSCfg:
   split_k: int = 1             # K splits per output tile (fp32 partial sums reduced in-kernel by the last split);
                                # -1 = chosen per shape (only shapes with few tiles and long K are split)
   k_serpentine: bool = True    # alternate the K direction from tile to tile of a cluster (L2 reuse across waves)
+  b_nmajor: bool | None = None # build_gemm_ws reads B[K,N] as given (MN-major tcgen05 operand) instead of making
+                               # the K-major copy BT (gemm.py:382): True = wherever the tile allows it, False = never,
+                               # None = for CTA-pair tiles only (see reads_b_directly)
 
   def __post_init__(self):
     if self.BK != 64: raise ValueError("BK must be 64 (one 128-byte swizzle atom)")
@@ -194,6 +197,15 @@ class WSCfg:
   @property
   def smem_bytes(self): return self.fixed_bytes + self.stage_bytes * self.stages_used
   @property
+  def reads_b_directly(self):
+    """True when build_gemm_ws hands B[K,N] to the kernel without a transposed copy. N-major B arrives in 64-column
+    boxes, so each CTA's share of a tile's columns (and of a half-width tail tile's) must be whole boxes. By default
+    (b_nmajor=None) only CTA pairs read B directly: on a B200 their kernel time is the same with either layout, while
+    single-CTA tiles ran 2-10 % slower with N-major B (Nsight Compute, 1024^3-8192^3)."""
+    if self.b_nmajor is False or (self.b_nmajor is None and not self.paired): return False
+    share = self.BN // 2 if self.paired else self.BN
+    return share % 64 == 0 and (self.n_mma == 2 or not self.split_tail or (share // 2) % 64 == 0)
+  @property
   def name(self):
     st = self.stages if self.stages is not None else "A"
     sm = self.num_sm if self.num_sm is not None else "dev"
@@ -201,16 +213,18 @@ class WSCfg:
             f"{'_tmast' if self.tma_store else ''}{'_hil' if self.hilbert else ''}"
             f"{f'_r{self.regs[0]}x{self.regs[1]}' if self.regs else ''}{f'_cl{self.cluster}' if self.cluster > 1 else ''}"
             f"{f'_x{self.n_mma}' if self.n_mma > 1 else ''}{f'_sk{self.split_k}' if self.split_k > 1 else '_skA' if self.split_k == -1 else ''}"
-            f"{'' if self.k_serpentine else '_kfwd'}")
+            f"{'' if self.k_serpentine else '_kfwd'}{'' if self.b_nmajor is None else '_bN' if self.b_nmajor else '_bT'}")
 
   def to_c(self, kind: int = _capi.KIND_WS, num_sm: int | None = None, wait_budget_ns: int = 0,
-           debug_skip_job: int = -1) -> _capi.BgCfg:
+           debug_skip_job: int = -1, b_nmajor: bool = False) -> _capi.BgCfg:
+    """The C-ABI config. ``b_nmajor`` says how the caller passes B: B[K,N] itself (True) or BT[N,K] (False)."""
     return _capi.BgCfg(kind=kind, BN=self.BN, BK=self.BK, stages=self.stages or 0, consumers=self.consumers,
                        num_sm=num_sm or self.num_sm or 0, group_m=self.group_m, group_n=self.group_n,
                        tma_store=int(self.tma_store), cluster=self.cluster, hilbert=int(self.hilbert),
                        acc_bufs=self.acc_bufs or 0, wait_budget_ns=wait_budget_ns, debug_skip_job=debug_skip_job,
                        n_mma=self.n_mma, no_tail_split=0 if self.split_tail else 1, ragged=int(self.ragged),
-                       split_k=self.split_k, no_k_serpentine=0 if self.k_serpentine else 1)
+                       split_k=self.split_k, no_k_serpentine=0 if self.k_serpentine else 1,
+                       b_nmajor=int(b_nmajor))
 
 
 # =============================================================================================================
@@ -245,6 +259,22 @@ def plan_gemm_bt(A, BT, Cout, cfg: WSCfg, *, wait_budget_ns: int = 0, debug_skip
   return _make_launch(plan, lambda: current_stream(Cout), Cout, (A, BT, Cout))
 
 
+def plan_gemm_b(A, B, Cout, cfg: WSCfg, *, wait_budget_ns: int = 0, debug_skip_job: int = -1):
+  """C[M,N] = A[M,K] @ B[K,N] with B read N-major as it is (no copy). B and C may be column views of wider
+  matrices (their row pitches are passed to the kernel), so a rank's shard B[:, c0:c1] needs no copy either.
+  Each CTA's share of the tile's columns must be a multiple of 64 (``cfg.reads_b_directly``). Returns ``launch``."""
+  a, b, c = operand(A), operand(B), operand(Cout)
+  M, K = a.shape
+  N = b.shape[1]
+  if b.shape != (K, N) or c.shape != (M, N): raise ValueError("A, B and C shapes do not match the GEMM")
+  if not (a.bf16 and b.bf16 and c.bf16): raise ValueError("A, B and C must be bfloat16")
+  if not (a.device == b.device == c.device): raise ValueError("A, B and C must be on the same device")
+  plan = _capi.Plan(cfg.to_c(_capi.KIND_WS, wait_budget_ns=wait_budget_ns, debug_skip_job=debug_skip_job,
+                             b_nmajor=True), M, N, K, a.ptr, a.row_pitch, b.ptr, b.row_pitch, c.ptr, c.row_pitch,
+                    a.device)
+  return _make_launch(plan, lambda: current_stream(Cout), Cout, (A, B, Cout))
+
+
 def build_gemm_ws(N: int, cfg: WSCfg, M: int | None = None, K: int | None = None, *, wait_budget_ns: int = 0,
                   debug_skip_job: int = -1):
   """C[M,N] = A[M,K] @ B[K,N] (square by default), bf16 in, fp32 accumulate, bf16 out.
@@ -273,6 +303,12 @@ def build_gemm_ws(N: int, cfg: WSCfg, M: int | None = None, K: int | None = None
     if a.shape != (M, K) or b.shape != (K, N) or c.shape != (M, N): raise ValueError("A, B and C shapes do not match the GEMM")
     if not (a.bf16 and b.bf16 and c.bf16): raise ValueError("A, B and C must be bfloat16")
     if not (a.device == b.device == c.device): raise ValueError("A, B and C must be on the same device")
+    if cfg.reads_b_directly:
+      # B as given, N-major: no transposed copy (the reference makes one per run, gemm.py:382)
+      plan = _capi.Plan(cfg.to_c(_capi.KIND_WS, wait_budget_ns=wait_budget_ns, debug_skip_job=debug_skip_job,
+                                 b_nmajor=True), M, N, K, a.ptr, a.row_pitch, b.ptr, b.row_pitch, c.ptr, c.row_pitch,
+                        a.device)
+      return _make_launch(plan, lambda: current_stream(Cout), Cout, (A, B, Cout))
     BT = transpose_contiguous(B)          # K-major B. Keep it alive: the tensor map holds its raw device pointer
     bt = operand(BT)
     plan = _capi.Plan(cfg.to_c(_capi.KIND_WS, wait_budget_ns=wait_budget_ns, debug_skip_job=debug_skip_job), M, N, K,

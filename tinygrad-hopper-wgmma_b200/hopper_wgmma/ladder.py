@@ -65,8 +65,10 @@ EXTRA = {
 def lookup(name: str):
   """A config by name from LADDER, SWEEP, B200 or EXTRA, with optional ``@`` modifiers so that sweeps can vary one
   knob on any tile shape: ``@sk<S>`` sets ``split_k=S`` (``@skA`` = automatic), ``@reg`` selects the register
-  epilogue (``tma_store=False``), ``@s<N>`` sets the ring depth ``stages=N``. Example: ``cta_n128@sk2``,
-  ``cta_n64@reg@skA``, ``pair_n128@s4``."""
+  epilogue (``tma_store=False``), ``@s<N>`` sets the ring depth ``stages=N``, ``@bT`` makes build_gemm_ws copy B
+  to a K-major BT first (``b_nmajor=False``, the reference's operand layout) and ``@bN`` makes it read B[K,N]
+  directly wherever the tile allows (``b_nmajor=True``). Example: ``cta_n128@sk2``, ``cta_n64@reg@skA``,
+  ``pair_n128@s4``, ``cluster_hilbert@bT``, ``cta_n128@bN``."""
   import dataclasses
   base, *mods = name.split("@")
   cfg = {**LADDER, **SWEEP, **EXTRA, **B200}[base]
@@ -76,6 +78,8 @@ def lookup(name: str):
       cfg = dataclasses.replace(cfg, tma_store=False)
     elif mod.startswith("sk") and (mod[2:].isdigit() or mod[2:] == "A"):
       cfg = dataclasses.replace(cfg, split_k=-1 if mod[2:] == "A" else int(mod[2:]))
+    elif mod in ("bT", "bN"):
+      cfg = dataclasses.replace(cfg, b_nmajor=mod == "bN")
     elif mod.startswith("s") and mod[1:].isdigit():
       cfg = dataclasses.replace(cfg, stages=int(mod[1:]))
     else:
