@@ -540,9 +540,29 @@ __global__ void __launch_bounds__(kWsThreads, 1)
     const uint32_t my_stage = sC + static_cast<uint32_t>(q) * 2u * STAGE_C;
     const bool split = NB == 2 && p.acc_bufs == 1;
     uint32_t acc = 0, acc_phase = 0, chunk = 0;
+    // Free an accumulator buffer for the MMA warp once this warp's tensor-memory reads of it have completed. The
+    // arrive is relaxed: it hands back tensor memory and publishes no memory writes (C goes out through TMA stores
+    // or plain stores that no one in the kernel reads). A release arrive here stalled each epilogue warp about 3000
+    // cycles per 256-column half, which the MMA warp of a 256x512 pair tile waited out at every tile boundary. The
+    // cluster's last entry skips the arrive: no MMA waits for that buffer again, and in a pair the remote arrive
+    // would only delay the teardown (tensor memory is freed after the final CTA barrier, which also orders the last
+    // TMEM reads).
+    bool last_entry = false;
+    auto release = [&](uint32_t bar) {
+      if (last_entry) return;
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        if (PAIRED)
+          mbar_arrive_cluster_relaxed(mapa_shared(bar, 0));
+        else
+          mbar_arrive_local_relaxed(bar);
+      }
+    };
     // Write accumulator columns starting at TMEM address tacc (this warp's lanes) to C rows row0.., columns
-    // [ccol, ccol + ncols).
-    auto drain = [&](uint32_t tacc, int row0, int ccol, int ncols) {
+    // [ccol, ccol + ncols), and release accumulator barrier rel_bar (0 = none) as soon as the last columns are in
+    // registers, before their stores.
+    auto drain = [&](uint32_t tacc, int row0, int ccol, int ncols, uint32_t rel_bar) {
       if constexpr (TMA_STORE) {
         const int nchunks = ncols >> 6;
 #pragma unroll 1
@@ -551,6 +571,7 @@ __global__ void __launch_bounds__(kWsThreads, 1)
           tmem_ld_32x32b_x32(tacc + 64u * c, v0);
           tmem_ld_32x32b_x32(tacc + 64u * c + 32u, v1);
           tmem_ld_wait();
+          if (!SPLITK && c + 1 == nchunks && rel_bar != 0u) release(rel_bar);
           const uint32_t buf = my_stage + (chunk & 1u) * STAGE_C;
           if (lane == 0) bulk_wait_group_read<1>();   // the store issued from this buffer two chunks ago has read it
           __syncwarp();
@@ -576,24 +597,11 @@ __global__ void __launch_bounds__(kWsThreads, 1)
             bulk_commit_group();
           }
         }
+        if (SPLITK && rel_bar != 0u) release(rel_bar);   // (after the loop: no registers to spare in these kernels)
       } else {
         __nv_bfloat16* crow = p.C + static_cast<long long>(row0 + lane) * p.ldc + ccol;
         epilogue_registers(tacc, crow, ncols, lane < ROWS_W && row0 + lane < p.m_valid, p.n_valid - ccol);
-      }
-    };
-    // Free an accumulator buffer for the MMA warp. The cluster's last entry skips it: no MMA waits for that buffer
-    // again, and in a pair the remote arrive would only delay the teardown (tensor memory is freed after the final
-    // CTA barrier, which also orders the last TMEM reads).
-    bool last_entry = false;
-    auto release = [&](uint32_t bar) {
-      if (last_entry) return;
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) {
-        if (PAIRED)
-          mbar_arrive_cluster(mapa_shared(bar, 0));
-        else
-          mbar_arrive_local(bar);
+        if (rel_bar != 0u) release(rel_bar);
       }
     };
     // Split-K (p.split_k > 1). The split_k entries of a tile run on different clusters, each into its own
@@ -791,7 +799,7 @@ __global__ void __launch_bounds__(kWsThreads, 1)
       if (sk_count()) {
         sk_reduce(tacc, 0, nch, staged, nullptr, false, 0);
         tmem_st_wait();
-        drain(tacc, row0, col0, nch * 32);
+        drain(tacc, row0, col0, nch * 32, 0u);
       }
       return true;
     };
@@ -818,8 +826,10 @@ __global__ void __launch_bounds__(kWsThreads, 1)
           tc_fence_after();
           if (SPLITK && p.split_k > 1) continue;   // both halves first, then the split-K epilogue on the whole tile
           const uint32_t tacc = tmem_base + lane_base + static_cast<uint32_t>(h * p.bn);
-          if (h == 0 || !narrow) drain(tacc, row0, col0 + h * p.bn, p.bn);
-          release(tempty0 + 8u * h);
+          if (h == 0 || !narrow)
+            drain(tacc, row0, col0 + h * p.bn, p.bn, tempty0 + 8u * h);
+          else
+            release(tempty0 + 8u * h);
         }
         if (!ok) break;
         if (SPLITK && p.split_k > 1) {
@@ -839,9 +849,9 @@ __global__ void __launch_bounds__(kWsThreads, 1)
       if (SPLITK && p.split_k > 1) {
         if (!sk_epilogue(idx, i, tacc, width >> 5, row0, col0)) break;
       } else {
-        drain(tacc, row0, col0, width);
+        drain(tacc, row0, col0, width, tempty0 + 8u * acc);
       }
-      release(tempty0 + 8u * acc);
+      if (SPLITK && p.split_k > 1) release(tempty0 + 8u * acc);
       if (++acc == static_cast<uint32_t>(p.acc_bufs)) {
         acc = 0;
         acc_phase ^= 1u;

@@ -80,6 +80,17 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_bar) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
 }
 
+// Arrives without release semantics, for hand-offs that publish no memory writes: the epilogue returning an
+// accumulator whose tensor-memory reads have completed (tcgen05.wait::ld, then tcgen05.fence::before_thread_sync).
+// A release arrive at cluster scope first waits for the thread's earlier memory operations to be performed at that
+// scope, which measured about 3000 cycles after an epilogue's shared-memory stores and TMA stores.
+__device__ __forceinline__ void mbar_arrive_cluster_relaxed(uint32_t cluster_bar) {
+  asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_local_relaxed(uint32_t bar) {
+  asm volatile("mbarrier.arrive.relaxed.cta.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
