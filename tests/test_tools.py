@@ -71,10 +71,12 @@ def test_best_config_by_size():
   from hopper_wgmma.ladder import B200, LADDER, best_config
   assert best_config(8192, 8192, 8192) is B200["pair_wide_hilbert"]
   assert best_config(32768, 4096, 32768) is B200["pair_wide_hilbert"]     # one rank of the 8-GPU 32768^3 shard
+  assert best_config(6144, 6144, 6144) is B200["pair_wide_hilbert"]
+  assert best_config(16384, 4096, 4096) is B200["pair_wide_hilbert"]
   assert best_config(4096, 4096, 4096) is LADDER["cluster_hilbert"]
   assert best_config(8192, 8192, 2048) is LADDER["cluster_hilbert"]       # short K: 256x256 pairs (104 % of cuBLAS)
   assert best_config(2048, 2048, 16384) is LADDER["cluster_hilbert"]
-  assert best_config(2048, 2048, 2048) is LADDER["hilbert"]
+  assert best_config(2048, 2048, 2048) is LADDER["cluster_hilbert"]
   small = best_config(1024, 1024, 8192)
   assert small.BN == 128 and small.cluster == 1 and small.split_k == -1
 

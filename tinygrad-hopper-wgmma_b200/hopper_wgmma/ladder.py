@@ -89,13 +89,12 @@ def lookup(name: str):
 
 def best_config(M: int, N: int, K: int) -> WSCfg:
   """The config the B200 ncu shape sweep found fastest for a problem of this size (results/summary.md):
-  256x512 CTA-pair tiles once the GEMM is big enough to run at the power cap (M*N*K >= 8192^3), where they move a
-  quarter fewer operand bytes per FLOP; 256x256 pair tiles from 3072^2 outputs up, or from 2048^2 with a long K; 128x256
-  CTA tiles at 2048^2; 128x128 CTA tiles below, with split-K chosen automatically (it splits only shapes with few
-  tiles and a long K). Tile-multiple shapes are assumed; pass ``ragged=True`` yourself otherwise."""
+  256x512 CTA-pair tiles once the GEMM is big enough to run at the power cap (M*N*K >= 6144^3), where they move a
+  quarter fewer operand bytes per FLOP; 256x256 pair tiles from 2048^2 outputs up; 128x128 CTA tiles below, with
+  split-K chosen automatically (it splits only shapes with few tiles and a long K). The pair tiles also read B as
+  given (no transposed copy in ``run``). Tile-multiple shapes are assumed; pass ``ragged=True`` yourself otherwise."""
   import dataclasses
-  if M * N * K >= 8192 ** 3: return B200["pair_wide_hilbert"]
-  if M * N >= 3072 * 3072 or (M * N >= 2048 * 2048 and K >= 4096): return LADDER["cluster_hilbert"]
-  if M * N >= 2048 * 2048: return LADDER["hilbert"]
+  if M * N * K >= 6144 ** 3: return B200["pair_wide_hilbert"]
+  if M * N >= 2048 * 2048: return LADDER["cluster_hilbert"]
   return dataclasses.replace(B200["cta_n128"], split_k=-1)
 
