@@ -3,7 +3,8 @@
 //
 // These replace the Hopper primitives the reference emits as strings (hopper_wgmma/gemm.py:38-140: mbar_init,
 // fence_mbar_init, mbar_expect_tx, mbar_arrive, mbar_arrive_cluster, mbar_wait, tma_load, cluster_sync, setmaxnreg)
-// and the wgmma helper of patches/0001-hopper-wgmma-uop.patch:129-207. Differences that matter:
+// and the wgmma helper of patches/0001-hopper-wgmma-uop.patch:129-207. The reference's consumer arrives become
+// tcgen05.commit (the MMA side) and relaxed arrives (the epilogue side). Differences that matter:
 //   * every mbarrier wait is bounded by a %globaltimer budget and reports failure instead of spinning forever
 //     (the reference's mbar_wait, gemm.py:73-78, spins without limit);
 //   * there is no TMA load with cluster multicast anywhere: a CTA pair shares operands through tcgen05's
@@ -71,19 +72,11 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t byt
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
 }
 
-__device__ __forceinline__ void mbar_arrive_local(uint32_t bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
-}
-
-// Arrive on a barrier addressed in the shared::cluster window (this CTA's or the peer's, via mapa_shared).
-__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_bar) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
-}
-
-// Arrives without release semantics, for hand-offs that publish no memory writes: the epilogue returning an
+// Plain arrives, without release semantics, for hand-offs that publish no memory writes: the epilogue returning an
 // accumulator whose tensor-memory reads have completed (tcgen05.wait::ld, then tcgen05.fence::before_thread_sync).
 // A release arrive at cluster scope first waits for the thread's earlier memory operations to be performed at that
-// scope, which measured about 3000 cycles after an epilogue's shared-memory stores and TMA stores.
+// scope, which measured about 3000 cycles after an epilogue's shared-memory stores and TMA stores. The cluster form
+// takes a barrier addressed in the shared::cluster window (this CTA's or the peer's, via mapa_shared).
 __device__ __forceinline__ void mbar_arrive_cluster_relaxed(uint32_t cluster_bar) {
   asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
 }
