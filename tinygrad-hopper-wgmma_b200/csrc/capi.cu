@@ -546,8 +546,8 @@ int32_t setup_plan(const bg_cfg& c, int64_t M, int64_t N, int64_t K, const void*
   // dealt table) is split into half-width tiles when twice its size still fits in one wave, so that the tail takes
   // about half a tile's time instead of a whole one. Half width = one N block when nblk == 2, MMA N = BN/2 otherwise.
   const int half = nblk == 2 ? bn : bn / 2;
-  const bool narrow_ok =
-      nblk == 2 || (half % 16 == 0 && (!c.tma_store || half % 64 == 0) && (!nmajor || (half / cl) % 64 == 0));
+  const bool narrow_ok = nblk == 2 || (half % 16 == 0 && (!c.tma_store || half % 64 == 0) &&
+                                       (!nmajor || (paired ? half / 2 : half) % 64 == 0));
   int64_t n_entries = tiles;
   if (c.kind == BG_KIND_WS && !c.no_tail_split && sk == 1 && narrow_ok && !sched.empty()) {
     const int64_t full = (tiles / nclusters) * nclusters;

@@ -262,7 +262,8 @@ def plan_gemm_bt(A, BT, Cout, cfg: WSCfg, *, wait_budget_ns: int = 0, debug_skip
 def plan_gemm_b(A, B, Cout, cfg: WSCfg, *, wait_budget_ns: int = 0, debug_skip_job: int = -1):
   """C[M,N] = A[M,K] @ B[K,N] with B read N-major as it is (no copy). B and C may be column views of wider
   matrices (their row pitches are passed to the kernel), so a rank's shard B[:, c0:c1] needs no copy either.
-  Each CTA's share of the tile's columns must be a multiple of 64 (``cfg.reads_b_directly``). Returns ``launch``."""
+  Each CTA's share of the tile's columns (BN, or BN / 2 in a CTA pair) must be a multiple of 64, or the plan raises
+  ValueError; half-width tail tiles are used only when their share is too. Returns ``launch``."""
   a, b, c = operand(A), operand(B), operand(Cout)
   M, K = a.shape
   N = b.shape[1]
