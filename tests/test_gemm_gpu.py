@@ -173,11 +173,13 @@ def _layout_cases():
     ("split_k4", WSCfg(BN=128, tma_store=True, split_k=4), (256, 256, 4096)),
     ("split_k2_wide_pair", WSCfg(n_mma=2, cluster=2, tma_store=True, split_k=2), (256, 1024, 2048)),
     ("serpentine_waves", WSCfg(n_mma=2, cluster=2, tma_store=True, num_sm=10), (1024, 2048, 640)),
+    # unpaired CTAs in clusters of 2 (BM = 64): each CTA loads the whole N block; the last wave is split
+    ("cluster2_unpaired_tail", WSCfg(consumers=1, cluster=2, BN=128, tma_store=True, num_sm=6), (640, 640, 192)),
   ]
 
 
 @pytest.mark.parametrize("layout", ["N", "K"])
-@pytest.mark.parametrize("idx", range(14))
+@pytest.mark.parametrize("idx", range(15))
 def test_b_operand_layouts(idx, layout, cuda_dev):
   import dataclasses
   from hopper_wgmma import build_gemm_ws
