@@ -1,8 +1,8 @@
 """Generate tests/golden/reference_host.json by running the reference's own host-side Python.
 
-Run in a container that has the reference checkout (default ``/root/reference``, or pass a path):
+Run in a container that has the reference checkout, passing its root:
 
-    python tests/golden/make_golden.py [REFERENCE_ROOT]
+    python tests/golden/make_golden.py REFERENCE_ROOT
 
 The reference package (hopper_wgmma/) imports tinygrad at module level, and tinygrad is not installable here. Its
 host logic (config dataclasses and their validation, the shape contract and kernel naming of build_gemm_ws /
@@ -173,7 +173,8 @@ def main(root: Path) -> dict:
 
 
 if __name__ == "__main__":
-  root = Path(sys.argv[1]) if len(sys.argv) > 1 else Path("/root/reference")
+  if len(sys.argv) != 2: raise SystemExit("usage: python tests/golden/make_golden.py REFERENCE_ROOT")
+  root = Path(sys.argv[1])
   data = main(root)
   (HERE / "reference_host.json").write_text(json.dumps(data, indent=1) + "\n")
   print(f"wrote {HERE / 'reference_host.json'}")

@@ -27,7 +27,7 @@ def build(N: int, cfg, M: int | None = None, K: int | None = None, **hooks):
   return build_gemm_ws(N, cfg, M, K, **hooks)
 
 
-# Extra tile shapes tried per problem shape by the sweep (BN=192 lets e.g. 3072 divide evenly over the CTAs).
+# Tile shapes the shape sweep adds to the ladder's: 192-column tiles split widths such as 3072 into whole tiles.
 SWEEP = {
   "tma_store": LADDER["tma_store"],
   "hilbert": LADDER["hilbert"],
@@ -88,7 +88,8 @@ def lookup(name: str):
 
 
 def best_config(M: int, N: int, K: int) -> WSCfg:
-  """The config the B200 ncu shape sweep found fastest for a problem of this size (results/summary.md):
+  """The config the B200 Nsight Compute shape sweep (``python -m hopper_wgmma.report ncu-sweep``) found fastest
+  for a problem of this size:
   256x512 CTA-pair tiles once the GEMM is big enough to run at the power cap (M*N*K >= 6144^3), where they move a
   quarter fewer operand bytes per FLOP; 256x256 pair tiles from 2048^2 outputs up; 128x128 CTA tiles below, with
   split-K chosen automatically (it splits only shapes with few tiles and a long K). The pair tiles also read B as
