@@ -173,11 +173,13 @@ void bg_plan_destroy(bg_plan* plan);
  * library, held until the process exits), so a problem may have at most 65536 tiles (cluster tiles of the schedule);
  * larger ones are rejected with a negative status before anything is enqueued.
  *   The first call on a device looks up the array's device address (cudaGetSymbolAddress) with that device current;
- *   make that first call before any stream capture.
+ *   make that first call before any stream capture. (A lookup that fails is retried by the next call.)
  *   Every call reuses the same array and overwrites the previous call's tile table and error word (the error word is
  *   cleared on the stream before each launch). Calls whose kernels can overlap on the GPU — on different streams, or
  *   from different threads — race on that array: serialize them on one stream.
- *   The tile table is copied from pageable host memory, so the call waits for work already queued on `stream`.
+ *   The tile table is staged from host memory with cudaMemcpyAsync on `stream`, ordered after the stream's earlier
+ *   work.
+ *   split_k: values above 1 are rejected (a split schedule needs a workspace); -1 (automatic) runs unsplit here.
  *   err_word == NULL: returns once the GEMM is enqueued. Otherwise it waits for `stream`, stores the kernel's error
  *   word (0 = ok) and returns a positive status if a device-side wait timed out.
  */

@@ -710,11 +710,11 @@ constexpr int kNoAllocErrOffset = kNoAllocMaxTiles;   // int32 index of the erro
 static __device__ __align__(256) int32_t g_noalloc_scratch[kNoAllocMaxTiles + 64];
 
 // In host code g_noalloc_scratch names a host-side stand-in, not device memory: its device address is looked up
-// once per device, with that device current, and handed to the kernel.
+// with the device current, on the first call that succeeds in doing so, and handed to the kernel. A failed lookup
+// is not remembered, so a later call tries again.
 struct NoAllocScratch {
-  std::once_flag once;
+  std::mutex mu;
   int32_t* ptr = nullptr;
-  cudaError_t status = cudaSuccess;
 };
 
 NoAllocScratch& noalloc_scratch(int dev) {
@@ -733,34 +733,47 @@ int32_t bg_gemm_noalloc(const bg_cfg* cfg, int64_t M, int64_t N, int64_t K, cons
   if (device < 0 || device >= 64) return fail(-1, "device %d out of range", device);
   if (cfg->split_k > 1)
     return fail(-1, "bg_gemm_noalloc has no split-K workspace (split_k = %d); use bg_plan_create", cfg->split_k);
+  // The automatic choice (split_k = -1) would split some shapes (few tiles, long K), and a split schedule needs a
+  // workspace this entry point does not have: here those shapes run unsplit.
+  bg_cfg c = *cfg;
+  if (c.split_k == -1) c.split_k = 1;
   bg_plan plan;   // lives on this stack frame and owns no device memory
   std::vector<int32_t> sched;
   std::array<int, 8> sched_key{};
-  int32_t st = setup_plan(*cfg, M, N, K, A, lda, BT, ldb, C, ldc, device, &plan, sched, sched_key, true);
+  int32_t st = setup_plan(c, M, N, K, A, lda, BT, ldb, C, ldc, device, &plan, sched, sched_key, true);
   if (st) return st;
   DeviceGuard guard(device);
   if (guard.status != cudaSuccess) return cuda_fail(guard.status, "cudaSetDevice");
-  st = setup_plan(*cfg, M, N, K, A, lda, BT, ldb, C, ldc, device, &plan, sched, sched_key);
+  st = setup_plan(c, M, N, K, A, lda, BT, ldb, C, ldc, device, &plan, sched, sched_key);
   if (st) return st;
+  if (plan.kp.split_k > 1 || plan.partial_bytes > 0)   // never reached with split_k <= 1; kept as the guard
+    return fail(-1, "bg_gemm_noalloc: the plan needs a split-K workspace; use bg_plan_create");
   if (sched.size() > static_cast<size_t>(kNoAllocMaxTiles))
     return fail(-1, "bg_gemm_noalloc: %zu tiles exceed its fixed scratch of %d tile entries; use bg_plan_create or "
                 "wider tiles", sched.size(), kNoAllocMaxTiles);
-  NoAllocScratch& ns = noalloc_scratch(device);
-  std::call_once(ns.once, [&ns] {
-    ns.status = cudaGetSymbolAddress(reinterpret_cast<void**>(&ns.ptr), g_noalloc_scratch);
-  });
-  if (ns.status != cudaSuccess) return cuda_fail(ns.status, "cudaGetSymbolAddress(g_noalloc_scratch)");
+  int32_t* scratch = nullptr;
+  {
+    NoAllocScratch& ns = noalloc_scratch(device);
+    std::lock_guard<std::mutex> lock(ns.mu);
+    if (ns.ptr == nullptr) {
+      int32_t* ptr = nullptr;
+      const cudaError_t e = cudaGetSymbolAddress(reinterpret_cast<void**>(&ptr), g_noalloc_scratch);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(g_noalloc_scratch)");
+      ns.ptr = ptr;
+    }
+    scratch = ns.ptr;
+  }
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  unsigned int* err = reinterpret_cast<unsigned int*>(ns.ptr + kNoAllocErrOffset);
+  unsigned int* err = reinterpret_cast<unsigned int*>(scratch + kNoAllocErrOffset);
   cudaError_t e;
   if (!sched.empty()) {
-    // From pageable host memory: the copy waits for work already queued on the stream, and the table may be freed
-    // as soon as cudaMemcpyAsync returns.
-    e = cudaMemcpyAsync(ns.ptr, sched.data(), sched.size() * sizeof(int32_t), cudaMemcpyHostToDevice, s);
+    // Staged from host memory on the stream, ordered after the stream's earlier work; the host vector may go away
+    // once cudaMemcpyAsync has returned.
+    e = cudaMemcpyAsync(scratch, sched.data(), sched.size() * sizeof(int32_t), cudaMemcpyHostToDevice, s);
     if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyAsync(tile table)");
   }
   if ((e = cudaMemsetAsync(err, 0, sizeof(unsigned int), s)) != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync");
-  plan.kp.sched = sched.empty() ? nullptr : ns.ptr;
+  plan.kp.sched = sched.empty() ? nullptr : scratch;
   plan.kp.err = err;
   if ((st = bg_plan_launch(&plan, stream))) return st;
   if (err_word == nullptr) return 0;
