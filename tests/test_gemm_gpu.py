@@ -447,3 +447,36 @@ def test_split_k_auto_choice(cuda_dev):
   _, launch = run_case(lambda: build_gemm_ws(1024, cfg, 1024, 1024, wait_budget_ns=BUDGET_NS), 1024, 1024, 1024,
                        cuda_dev, reps=1)
   assert launch.info()["split_k"] == 1            # 16 k-blocks: too short to split
+
+
+def test_plan_tables_hold_bounded_device_memory(cuda_dev):
+  """Plans for 1000 distinct M values (a caller with ragged batch sizes): each plan's tile table is shared while a
+  plan uses it and freed (beyond a small idle cache) once none does, so device memory stays bounded; a shape whose
+  table was evicted on the way plans and computes correctly again."""
+  torch = _torch()
+  from hopper_wgmma import WSCfg, build_gemm_ws
+  from hopper_wgmma.gemm import plan_gemm_bt
+  cfg = WSCfg(tma_store=True, hilbert=True)           # 128 x 256 tiles, Hilbert table
+  small = lambda: build_gemm_ws(512, cfg, 512, 320, wait_budget_ns=BUDGET_NS)
+  worst, _ = run_case(small, 512, 512, 320, cuda_dev, reps=1)   # its table goes idle when the plan is dropped
+  assert worst <= TOL
+  N, K, M_max = 4096, 64, 128 * 2000
+  A = torch.zeros((M_max, K), dtype=torch.bfloat16, device=cuda_dev)
+  BT = torch.zeros((N, K), dtype=torch.bfloat16, device=cuda_dev)
+  C = torch.zeros((M_max, N), dtype=torch.bfloat16, device=cuda_dev)
+
+  def plans(lo, hi):
+    for i in range(lo, hi):
+      M = 128 * (1000 + i)                            # 1000-2000 row tiles x 16 column tiles: 64-128 KB tables
+      launch = plan_gemm_bt(A[:M], BT, C[:M], cfg)
+      del launch
+  plans(0, 100)
+  torch.cuda.synchronize(cuda_dev)
+  free_warm = torch.cuda.mem_get_info(cuda_dev)[0]
+  plans(100, 1000)
+  torch.cuda.synchronize(cuda_dev)
+  free_after = torch.cuda.mem_get_info(cuda_dev)[0]
+  # unbounded, 900 more tables of 64-128 KB would take ~90 MB
+  assert free_warm - free_after < (24 << 20), (free_warm, free_after)
+  worst, _ = run_case(small, 512, 512, 320, cuda_dev, reps=1)
+  assert worst <= TOL

@@ -241,6 +241,31 @@ def test_cpp_hilbert_order_deals_like_reference(golden):
       assert [v for c in dealt for v in c] == case["ok"]
 
 
+def test_pruned_hilbert_walks_match_the_full_square_walk():
+  """The C++ and Python builders skip curve blocks outside the grid; the order must stay the one the full-square
+  walk of the reference (gemm.py:222-235, restated in oracle/schedule_ref.py) gives, on square, tall and wide
+  grids."""
+  import itertools
+  from hopper_wgmma import _capi
+  from hopper_wgmma.gemm import hilbert_order
+  from oracle import schedule_ref
+  for M, N in itertools.chain(itertools.product((1, 2, 3, 5, 8, 13, 31, 33, 64, 100), (1, 2, 3, 4, 9, 17, 40)),
+                              [(257, 1), (1, 300), (130, 7), (6, 129)]):
+    full = schedule_ref.hilbert_curve(M, N)
+    assert _capi.hilbert_order(M, N) == full, (M, N)
+    assert hilbert_order(M, N) == full, (M, N)
+
+
+def test_tall_grid_schedule_is_cheap():
+  """2^20 rows of 128-row tiles and one column tile: the full-square walk would visit 8192^2 = 67 M cells."""
+  import time
+  from hopper_wgmma import _capi
+  t0 = time.perf_counter()
+  curve = _capi.hilbert_order(8192, 1)
+  assert time.perf_counter() - t0 < 0.05
+  assert sorted(e >> 16 for e in curve) == list(range(8192))
+
+
 def test_cpp_and_python_grouped_orders_match_reference(golden):
   from hopper_wgmma import _capi
   from hopper_wgmma.gemm import grouped_tile_order

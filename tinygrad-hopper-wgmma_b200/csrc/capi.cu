@@ -97,15 +97,29 @@ void hilbert_d2xy(int n, long long d, int& x, int& y) {
   }
 }
 
+// The curve covers each aligned s x s block (s a power of two) in one run of s * s consecutive positions, so a run
+// whose block lies outside the grid is skipped whole: the walk costs O(cells of the grid * log dim) instead of
+// O(dim^2), which matters for tall or wide grids (2^20 rows of 128 give dim = 8192 for a single column of tiles).
+void hilbert_walk(int dim, long long d0, int s, int mt, int nt, std::vector<int32_t>& out) {
+  int x, y;
+  hilbert_d2xy(dim, d0, x, y);   // a cell of the block; its corner is (x, y) rounded down to multiples of s
+  if ((x & ~(s - 1)) >= mt || (y & ~(s - 1)) >= nt) return;
+  if (s == 1) {
+    out.push_back((x << 16) | y);
+    return;
+  }
+  const long long quarter = static_cast<long long>(s / 2) * (s / 2);
+  for (int i = 0; i < 4; ++i) hilbert_walk(dim, d0 + i * quarter, s / 2, mt, nt, out);
+}
+
+// Cells of the mt x nt grid in the order the Hilbert curve over the smallest power-of-two square covering it visits
+// them (gemm.py:218-240 walks every cell of that square and keeps the ones inside the grid: the same order).
 void hilbert_order(int mt, int nt, std::vector<int32_t>& out) {
   out.clear();
+  out.reserve(static_cast<size_t>(mt) * nt);
   int dim = 1;
   while (dim < std::max(mt, nt)) dim *= 2;
-  for (long long i = 0; i < static_cast<long long>(dim) * dim; ++i) {
-    int x, y;
-    hilbert_d2xy(dim, i, x, y);
-    if (x < mt && y < nt) out.push_back((x << 16) | y);
-  }
+  hilbert_walk(dim, 0, dim, mt, nt, out);
 }
 
 // grouped_tile_order (gemm.py:200-215): GM x GN super-tiles in row-major order when they divide the grid, else
@@ -187,6 +201,8 @@ struct bg_plan {
   int narrow_tiles = 0;
   GemmParams kp{};
   int32_t* d_sched = nullptr;
+  bool holds_table = false;          // d_sched is a reference on the device store's table table_key
+  std::array<int, 8> table_key{};
   unsigned int* d_err = nullptr;
   size_t partial_bytes = 0;          // split-K workspace, owned by the plan
   size_t ticket_words = 0;
@@ -218,11 +234,25 @@ struct DeviceGuard {
 
 // Device storage shared by the plans of one device, so that building a plan allocates nothing once warm (no
 // cudaMalloc / cudaFree, which can synchronize the device, on the path of a caller that plans per batch):
-//   * tile tables, one per distinct schedule, uploaded on first use and kept for the life of the process;
+//   * tile tables, one per distinct schedule, uploaded on first use and shared by every plan of that schedule
+//     (reference-counted). A table no plan uses stays cached for the next plan of its schedule, up to
+//     kIdleTables tables and kIdleTableBytes bytes per device; beyond that the least recently released ones are
+//     freed, so a caller whose shapes keep changing (ragged batches) holds bounded device memory;
 //   * error words, one per live plan, handed out from 4 KiB slabs and returned when the plan is destroyed.
+constexpr size_t kIdleTables = 64;
+constexpr size_t kIdleTableBytes = size_t{16} << 20;
+
+struct TableEntry {
+  int32_t* ptr = nullptr;
+  size_t bytes = 0;
+  int refs = 0;             // live plans using the table
+  uint64_t released = 0;    // when the last plan let go of it (store clock), for eviction order
+};
+
 struct DeviceStore {
   std::mutex mu;
-  std::map<std::array<int, 8>, int32_t*> tables;
+  std::map<std::array<int, 8>, TableEntry> tables;
+  uint64_t clock = 0;
   std::vector<unsigned int*> free_words;
 };
 
@@ -231,25 +261,63 @@ DeviceStore& device_store(int dev) {
   return stores[dev & 63];
 }
 
-int32_t store_table(int dev, const std::array<int, 8>& key, const std::vector<int32_t>& host, int32_t** out) {
+// Free idle tables, least recently released first, until the idle ones fit the caps. Called with s.mu held and
+// the store's device current.
+void evict_idle_tables(DeviceStore& s) {
+  for (;;) {
+    size_t idle = 0, idle_bytes = 0;
+    auto oldest = s.tables.end();
+    for (auto it = s.tables.begin(); it != s.tables.end(); ++it) {
+      if (it->second.refs > 0) continue;
+      ++idle;
+      idle_bytes += it->second.bytes;
+      if (oldest == s.tables.end() || it->second.released < oldest->second.released) oldest = it;
+    }
+    if (idle <= kIdleTables && idle_bytes <= kIdleTableBytes) return;
+    cudaFree(oldest->second.ptr);   // waits for work in flight, which may still read it
+    s.tables.erase(oldest);
+  }
+}
+
+// The device copy of schedule `key` (uploaded from `host` on first use), with one more reference on it.
+int32_t acquire_table(int dev, const std::array<int, 8>& key, const std::vector<int32_t>& host, int32_t** out) {
   DeviceStore& s = device_store(dev);
   std::lock_guard<std::mutex> lock(s.mu);
   auto it = s.tables.find(key);
   if (it != s.tables.end()) {
-    *out = it->second;
+    ++it->second.refs;
+    *out = it->second.ptr;
     return 0;
   }
   int32_t* d = nullptr;
-  cudaError_t e = cudaMalloc(&d, host.size() * sizeof(int32_t));
+  const size_t bytes = host.size() * sizeof(int32_t);
+  cudaError_t e = cudaMalloc(&d, bytes);
   if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(tile table)");
-  e = cudaMemcpy(d, host.data(), host.size() * sizeof(int32_t), cudaMemcpyHostToDevice);
+  e = cudaMemcpy(d, host.data(), bytes, cudaMemcpyHostToDevice);
   if (e != cudaSuccess) {
     cudaFree(d);
     return cuda_fail(e, "cudaMemcpy(tile table)");
   }
-  s.tables.emplace(key, d);
+  TableEntry entry;
+  entry.ptr = d;
+  entry.bytes = bytes;
+  entry.refs = 1;
+  s.tables.emplace(key, entry);
   *out = d;
   return 0;
+}
+
+// Drop one reference on schedule `key`'s table; idle tables beyond the caps are freed.
+void release_table(int dev, const std::array<int, 8>& key) {
+  DeviceStore& s = device_store(dev);
+  std::lock_guard<std::mutex> lock(s.mu);
+  auto it = s.tables.find(key);
+  if (it == s.tables.end()) return;
+  if (--it->second.refs <= 0) {
+    it->second.refs = 0;
+    it->second.released = ++s.clock;
+    evict_idle_tables(s);
+  }
 }
 
 int32_t take_error_word(int dev, unsigned int** out) {
@@ -272,10 +340,11 @@ int32_t take_error_word(int dev, unsigned int** out) {
 
 void free_plan(bg_plan* p) {
   if (p == nullptr) return;
-  if (p->d_partial || p->d_tickets) {
+  if (p->d_partial || p->d_tickets || p->holds_table) {
     DeviceGuard guard(p->device);
     if (p->d_partial) cudaFree(p->d_partial);
     if (p->d_tickets) cudaFree(p->d_tickets);
+    if (p->holds_table) release_table(p->device, p->table_key);
   }
   if (p->d_err) {
     DeviceStore& s = device_store(p->device);
@@ -675,7 +744,11 @@ int32_t bg_plan_create(bg_plan** out, const bg_cfg* cfg, int64_t M, int64_t N, i
   st = setup_plan(*cfg, M, N, K, A, lda, BT, ldb, C, ldc, device, p.get(), sched, sched_key);
   if (st) return st;
   // ---- device buffers: tile table (cached per schedule) and error word (from the device's slab)
-  if (!sched.empty() && (st = store_table(device, sched_key, sched, &p->d_sched))) return st;
+  if (!sched.empty()) {
+    if ((st = acquire_table(device, sched_key, sched, &p->d_sched))) return st;
+    p->holds_table = true;
+    p->table_key = sched_key;
+  }
   if ((st = take_error_word(device, &p->d_err))) return st;
   if (p->partial_bytes > 0) {
     // split-K workspace: partial sums (fully written before they are read) and zeroed arrival words

@@ -97,13 +97,23 @@ def _hilbert_d2xy(n: int, d: int) -> tuple[int, int]:
 
 
 def hilbert_order(M: int, N: int) -> list[int]:
-  """Tiles of an M x N tile grid in Hilbert-curve order, as (m << 16) | n."""
+  """Tiles of an M x N tile grid in Hilbert-curve order, as (m << 16) | n: the order in which the curve over the
+  smallest power-of-two square covering the grid visits them (gemm.py:222-235 walks the whole square and keeps the
+  cells inside the grid). The curve covers each aligned s x s block in one run of s * s positions, so runs whose
+  block lies outside the grid are skipped whole and tall or wide grids cost O(cells * log dim), not O(dim^2)."""
   dim = 1
   while dim < max(M, N): dim *= 2
-  out = []
-  for i in range(dim * dim):
-    x, y = _hilbert_d2xy(dim, i)
-    if x < M and y < N: out.append((x << 16) | y)
+  out: list[int] = []
+  stack = [(0, dim)]                     # (first curve position of a block, block side), visited in curve order
+  while stack:
+    d0, s = stack.pop()
+    x, y = _hilbert_d2xy(dim, d0)
+    if (x & ~(s - 1)) >= M or (y & ~(s - 1)) >= N: continue
+    if s == 1:
+      out.append((x << 16) | y)
+      continue
+    q = (s // 2) * (s // 2)
+    stack.extend((d0 + i * q, s // 2) for i in (3, 2, 1, 0))
   return out
 
 
@@ -137,7 +147,8 @@ class WSCfg:
   group_m: int = 16            # L2 tile order, super-tiles of group_m x group_n tiles
   group_n: int = 8
   tma_store: bool = False      # swizzled shared-memory staging + TMA store epilogue
-  regs: tuple[int, int] | None = None   # register split (producer, consumer); validated, see DESIGN notes
+  regs: tuple[int, int] | None = None   # register split (producer, consumer): validated, not applied (the
+                                        # kernels need <= 100 registers per thread without it)
   cluster: int = 1             # 2: two CTAs share one M = 256 MMA (cta_group::2), each loading half of B
   hilbert: bool = False        # Hilbert tile order from a host-built table
   acc_bufs: int | None = None  # accumulator buffers in tensor memory; None = 2 when 2 * width <= 512 columns
