@@ -1,6 +1,7 @@
 """Benchmark of the B200 bf16 GEMM (the hot path of narain1/tinygrad-hopper-wgmma) — prints ONE JSON line.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload NAME] [--cfg NAME]
+                    [--no-extra-legs] [--no-cpu-baseline] [--no-e2e]
 
 Workloads (per rank; one process per GPU, launched by torch.distributed.run for N > 1):
   gemm4096   (default) M=N=K=4096, the reference's ladder headline. With N GPUs each rank computes its own
@@ -10,7 +11,15 @@ Workloads (per rank; one process per GPU, launched by torch.distributed.run for 
   shard32k   M=N=K=32768 split by columns over the N GPUs (32768 x 32768/N x 32768 per rank): scaling "strong".
 A step is one GEMM launch on resident inputs. Between timed steps a 256 MiB buffer is rewritten to flush the 126 MB
 L2, and each step is timed alone with CUDA events on the launching stream; the whole timed region is bracketed by a
-barrier and a synchronize, and the reported time is the max over ranks. Throughput = 2*M*N*K of all ranks / time.
+barrier and a synchronize, and the reported time is the max over ranks. Throughput = 2*M*N*K of all ranks / time,
+with time = the mean step time (every throughput in the line, cuBLAS's included, uses the mean).
+
+Besides the main workload the line carries two more legs of the BASELINE configs, each with its own cuBLAS
+comparison, parity gate, roofline and clocks: ``gemm8192`` (one GPU only) and ``shard32k`` (at every N: the
+32768^3 GEMM split by columns over the N GPUs, strong scaling, with per-rank clocks). Every leg first runs once on
+NaN-poisoned C and is compared with the fp32 product of the same bf16 inputs (cuBLAS fp32, TF32 off); if any leg
+misses max|C - ref| / max|ref| <= 4e-3 or leaves a NaN, the line is still printed and the process exits with
+status 3.
 
 ``--impl reference`` times the reference's CPU path instead: its host reference ``a.float() @ b.float()``
 (scripts/smoke.py:41), fp32 accumulate over bf16 inputs plus the bf16 output rounding, on this host's cores
@@ -30,25 +39,29 @@ from pathlib import Path
 ROOT = Path(__file__).resolve().parent
 sys.path[:0] = [str(ROOT / "tinygrad-hopper-wgmma_b200"), str(ROOT)]
 
-METRIC = "bf16 GEMM TFLOPS at N=4096/8192 (ncu-timed), % of B200 dense peak and of cuBLAS"
+METRIC = "bf16 GEMM TFLOPS at N=4096/8192, % of B200 dense peak and of cuBLAS"
 WORKLOADS = {"gemm4096": (4096, 4096, 4096, "weak"), "gemm8192": (8192, 8192, 8192, "weak"),
              "shard32k": (32768, 32768, 32768, "strong")}
 FLUSH_BYTES = 256 << 20
 CPU_SAMPLE_SECONDS = 10.0
 REFERENCE_BUDGET_S = 90.0
+TOL = 4e-3              # max|C - ref| / max|ref| against the fp32 product (north_star tolerance)
+EXTRA_LEG_STEPS = 20    # timed steps of the gemm8192 / shard32k legs (fewer when --steps is smaller)
+GATE_FAILED_EXIT = 3
 
 
-def parse_args():
+def parse_args(argv=None):
   ap = argparse.ArgumentParser()
   ap.add_argument("--gpus", type=int, default=1)
-  ap.add_argument("--steps", type=int, default=2000)
-  ap.add_argument("--warmup", type=int, default=20)
+  ap.add_argument("--steps", type=int, default=200)
+  ap.add_argument("--warmup", type=int, default=10)
   ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
   ap.add_argument("--workload", choices=tuple(WORKLOADS), default="gemm4096")
   ap.add_argument("--cfg", default="best")
+  ap.add_argument("--no-extra-legs", action="store_true", help="time the main workload only")
   ap.add_argument("--no-cpu-baseline", action="store_true")
   ap.add_argument("--no-e2e", action="store_true")
-  return ap.parse_args()
+  return ap.parse_args(argv)
 
 
 def shapes(workload: str, world: int):
@@ -77,6 +90,25 @@ def profiled_traffic(kernel_tag: str, workload: str, flops_per_launch: float):
   return None
 
 
+def parity_gate(C, ref):
+  """Compare the bf16 output C with the fp32 reference product ``ref`` (same device): max|C - ref| / max|ref| and
+  the NaN count (C was NaN-poisoned before the launch). ``ok`` is False when either misses the bar."""
+  import torch
+  nan = int(torch.isnan(C).sum())
+  rel = float((C.float() - ref).abs().max() / (ref.abs().max() + 1e-9))
+  if rel != rel: rel = float("inf")
+  return {"rel_err_vs_fp32": rel, "nan_after_poison": nan, "tol": TOL, "ok": bool(nan == 0 and rel <= TOL)}
+
+
+def gates_failed(line: dict) -> list[str]:
+  """Names of the legs of a result line whose parity gate failed."""
+  bad = [] if line.get("parity", {}).get("ok", False) else ["main"]
+  for leg in ("gemm8192", "shard32k"):
+    sub = line.get(leg)
+    if isinstance(sub, dict) and "parity" in sub and not sub["parity"].get("ok", False): bad.append(leg)
+  return bad
+
+
 # ------------------------------------------------------------------------------------------------------------------
 # clocks during the timed region (NVML reads only; no setting is changed)
 # ------------------------------------------------------------------------------------------------------------------
@@ -85,7 +117,7 @@ class ClockSampler:
              "sync_boost": 0x10, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40, "hw_power_brake_slowdown": 0x80,
              "display_clock_setting": 0x100}
 
-  def __init__(self, device_index: int, period_s: float = 0.01):
+  def __init__(self, device_index: int, period_s: float = 0.002):
     self.samples, self.reasons, self.period, self.ok = [], 0, period_s, False
     self._stop = threading.Event()
     try:
@@ -98,17 +130,21 @@ class ClockSampler:
     except Exception as exc:   # NVML missing: report that instead of clocks
       self.err = repr(exc)
 
+  def _sample(self):
+    try:
+      self.samples.append(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
+      self.reasons |= self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+    except Exception:
+      pass
+
   def _run(self):
     while not self._stop.is_set():
-      try:
-        self.samples.append(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
-        self.reasons |= self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
-      except Exception:
-        pass
+      self._sample()
       time.sleep(self.period)
 
   def __enter__(self):
     if self.ok:
+      self._sample()
       self.t = threading.Thread(target=self._run, daemon=True)
       self.t.start()
     return self
@@ -117,6 +153,7 @@ class ClockSampler:
     if self.ok:
       self._stop.set()
       self.t.join()
+      self._sample()
 
   def summary(self) -> dict:
     if not self.ok: return {"error": self.err}
@@ -202,207 +239,285 @@ def pick_cfg(name: str, m: int, n: int, k: int):
     raise SystemExit(f"unknown --cfg {name}: {exc}")
 
 
-def run_ours(args):
-  import torch
-  import torch.distributed as dist
+def kernel_tag(info: dict, cfg) -> str:
+  return (f"sm100_gemm_ws_{'pair' if info['paired'] else 'cta'}_{'tmast' if cfg.tma_store else 'reg'}"
+          f"{'_x2' if cfg.n_mma == 2 else ''}")
 
-  from hopper_wgmma import shard
-  from hopper_wgmma.gemm import build_gemm_ws
 
-  rank, world = int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1"))
-  local = int(os.environ.get("LOCAL_RANK", "0"))
-  if world != args.gpus: raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
-  torch.cuda.set_device(local)
-  dev = torch.device("cuda", local)
-  if world > 1:
-    from datetime import timedelta
-    dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+class Bench:
+  """One rank's benchmark state: device, process group helpers and the L2-flush buffer."""
 
-  def barrier():
-    if world > 1: dist.barrier()
+  def __init__(self, args):
+    import torch
+    import torch.distributed as dist
+    self.torch, self.dist, self.args = torch, dist, args
+    self.rank, self.world = int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1"))
+    self.local = int(os.environ.get("LOCAL_RANK", "0"))
+    if self.world != args.gpus: raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={self.world}")
+    torch.cuda.set_device(self.local)
+    self.dev = torch.device("cuda", self.local)
+    if self.world > 1:
+      from datetime import timedelta
+      dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=self.dev)
+    self.flush = torch.empty(FLUSH_BYTES // 4, dtype=torch.int32, device=self.dev)
+    self.peaks = measured_peaks()
 
-  M, n, K, N_total, scaling = shapes(args.workload, world)
-  cfg_name, cfg = pick_cfg(args.cfg, M, n, K)
-  flops_rank = 2.0 * M * n * K
+  def barrier(self):
+    if self.world > 1: self.dist.barrier()
 
-  # inputs resident in HBM: A replicated (same seed everywhere), this rank's K-major B shard, this rank's C shard
-  g = torch.Generator(device=dev).manual_seed(1234)
-  A = torch.randn((M, K), generator=g, device=dev, dtype=torch.float32).to(torch.bfloat16)
-  gb = torch.Generator(device=dev).manual_seed(5678 + rank)
-  BT = torch.randn((n, K), generator=gb, device=dev, dtype=torch.float32).to(torch.bfloat16)
-  C = torch.full((M, n), float("nan"), dtype=torch.bfloat16, device=dev)
-  flush = torch.empty(FLUSH_BYTES // 4, dtype=torch.int32, device=dev)
-  launch = shard.local_gemm(A, BT, C, cfg)
-  info = launch.info()
+  def max_over_ranks(self, v: float) -> float:
+    if self.world == 1: return v
+    from hopper_wgmma import shard
+    return shard.max_over_ranks(v, device=self.dev)
 
-  def timed(fn, steps):
-    """Per-step device time (ms) with an L2 flush before every step, plus the max over ranks of the total."""
+  def gather(self, values: list[float]) -> list[list[float]]:
+    """Every rank's list of floats (same length on all ranks), in rank order."""
+    torch = self.torch
+    t = torch.tensor(values, dtype=torch.float64, device=self.dev)
+    if self.world == 1: return [values]
+    out = [torch.empty_like(t) for _ in range(self.world)]
+    self.dist.all_gather(out, t)
+    return [o.tolist() for o in out]
+
+  def timed(self, fn, steps):
+    """Per-step device times (ms) with an L2 flush before every step; returns (max over ranks of the total, list)."""
+    torch = self.torch
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
-    barrier()
+    self.barrier()
     torch.cuda.synchronize()
     for i in range(steps):
-      flush.zero_()
+      self.flush.zero_()
       starts[i].record()
       fn()
       ends[i].record()
     torch.cuda.synchronize()
-    barrier()
+    self.barrier()
     per = [s.elapsed_time(e) for s, e in zip(starts, ends)]
-    total = sum(per)
-    if world > 1: total = shard.max_over_ranks(total, device=dev)
-    return total, per
+    return self.max_over_ranks(sum(per)), per
 
-  # correctness gate on the benchmark's own inputs before timing (poisoned C, cuBLAS comparison)
-  launch()
-  launch.check()
-  ref = (A @ BT.t()).float()
-  rel = float((C.float() - ref).abs().max() / (ref.abs().max() + 1e-9))
-  equal = float((C.float() == ref).float().mean())   # fraction bitwise equal to cuBLAS's bf16 output
-  nan = int(torch.isnan(C).sum())
-  del ref
+  def interleaved(self, ours, cublas, steps):
+    """Ours and cuBLAS alternating launch by launch (same clocks, same flush protocol): mean ms of each, max over
+    ranks, plus the medians for reference."""
+    torch = self.torch
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(steps)]
+    self.barrier()
+    torch.cuda.synchronize()
+    for e in ev:
+      self.flush.zero_()
+      e[0].record()
+      ours()
+      e[1].record()
+      self.flush.zero_()
+      e[2].record()
+      cublas()
+      e[3].record()
+    torch.cuda.synchronize()
+    self.barrier()
+    o = [e[0].elapsed_time(e[1]) for e in ev]
+    c = [e[2].elapsed_time(e[3]) for e in ev]
+    return {"ours_mean_ms": self.max_over_ranks(statistics.mean(o)),
+            "cublas_mean_ms": self.max_over_ranks(statistics.mean(c)),
+            "ours_median_ms": self.max_over_ranks(statistics.median(o)),
+            "cublas_median_ms": self.max_over_ranks(statistics.median(c))}
 
-  for _ in range(args.warmup): launch()
-  torch.cuda.synchronize()
-  with ClockSampler(local) as clocks:
-    total_ms, per = timed(launch, args.steps)
-  launch.check()
-  ms = total_ms / args.steps
-  value = flops_rank * world / (ms * 1e-3) / 1e12
-  peaks = measured_peaks()
-  achieved = flops_rank / (statistics.mean(per) * 1e-3) / 1e12
+  def leg(self, workload: str, cfg_name: str, steps: int, warmup: int, per_rank_clocks: bool = False):
+    """Time one GEMM workload: parity gate on poisoned C, ``steps`` flushed launches (the leg's value), cuBLAS
+    interleaved, roofline and clocks. Returns (result dict, launch, operands) — the operands stay alive for the
+    caller's end-to-end leg."""
+    torch = self.torch
+    from hopper_wgmma import shard
+    M, n, K, N_total, scaling = shapes(workload, self.world)
+    cfg_name, cfg = pick_cfg(cfg_name, M, n, K)
+    flops_rank = 2.0 * M * n * K
+    # inputs resident in HBM: A replicated (same seed everywhere), this rank's K-major B shard, this rank's C shard
+    g = torch.Generator(device=self.dev).manual_seed(1234)
+    A = torch.randn((M, K), generator=g, device=self.dev, dtype=torch.float32).to(torch.bfloat16)
+    gb = torch.Generator(device=self.dev).manual_seed(5678 + self.rank)
+    BT = torch.randn((n, K), generator=gb, device=self.dev, dtype=torch.float32).to(torch.bfloat16)
+    C = torch.full((M, n), float("nan"), dtype=torch.bfloat16, device=self.dev)
+    launch = shard.local_gemm(A, BT, C, cfg)
+    info = launch.info()
 
-  # cuBLAS on the same inputs and protocol (the bar the reference compares against), interleaved launch by launch
-  # with ours so that both see the same clocks; the ratio of medians is reported
-  pair_steps = min(args.steps, 200)
-  Cc = torch.empty_like(C)
-  cub = lambda: torch.matmul(A, BT.t(), out=Cc)
-  for _ in range(5): cub()
-  ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(pair_steps)]
-  barrier()
-  torch.cuda.synchronize()
-  for e in ev:
-    flush.zero_()
-    e[0].record()
+    # parity gate on the leg's own inputs, before timing: NaN-poisoned C against the fp32 product (TF32 off)
     launch()
-    e[1].record()
-    flush.zero_()
-    e[2].record()
-    cub()
-    e[3].record()
-  torch.cuda.synchronize()
-  barrier()
-  ours_med = statistics.median(e[0].elapsed_time(e[1]) for e in ev)
-  cub_med = statistics.median(e[2].elapsed_time(e[3]) for e in ev)
-  if world > 1:
-    ours_med = shard.max_over_ranks(ours_med, device=dev)
-    cub_med = shard.max_over_ranks(cub_med, device=dev)
-  cub_tflops = flops_rank * world / (cub_med * 1e-3) / 1e12
+    launch.check()
+    tf32 = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+      ref = A.float() @ BT.float().t()
+    finally:
+      torch.backends.cuda.matmul.allow_tf32 = tf32
+    parity = parity_gate(C, ref)
+    del ref
+    parity["ok"] = self.max_over_ranks(0.0 if parity["ok"] else 1.0) == 0.0   # every rank passed
+    cub_bf16 = A @ BT.t()
+    parity["bitwise_equal_fraction_vs_cublas"] = round(float((C == cub_bf16).float().mean()), 4)
+    del cub_bf16
+    torch.cuda.empty_cache()
 
-  # End to end through the public API, as a caller streaming batches would run it: every step copies its A and B
-  # from pinned host memory, runs the reference-facing operator build_gemm_ws(...)(A, B, C)() (plan and launch; B is
-  # read as given for CTA-pair tiles, copied K-major first otherwise) and copies C back to pinned host memory. Steps rotate over three streams and buffer sets (two when
-  # a set would exceed 1 GiB), so one step's host-to-device copies overlap earlier steps' GEMMs and device-to-host
-  # copies without queueing behind them on a shared stream.
-  e2e = None
-  if not args.no_e2e:
+    for _ in range(warmup): launch()
+    torch.cuda.synchronize()
+    with ClockSampler(self.local) as clocks:
+      total_ms, per = self.timed(launch, steps)
+    launch.check()
+    ms = total_ms / steps
+    value = flops_rank * self.world / (ms * 1e-3) / 1e12
+    achieved = flops_rank / (statistics.mean(per) * 1e-3) / 1e12
+
+    Cc = torch.empty_like(C)
+    cub = lambda: torch.matmul(A, BT.t(), out=Cc)
+    for _ in range(3): cub()
+    pair_steps = max(3, min(steps, 200))
+    with ClockSampler(self.local) as clocks_pair:
+      cmp = self.interleaved(launch, cub, pair_steps)
+    del Cc
+    peak = self.peaks["bf16_tflops"]
+    traffic = profiled_traffic(kernel_tag(info, cfg), workload, flops_rank)
+    res = {
+      "value": round(value, 3), "unit": "TFLOPS", "ms_per_step": round(ms, 5), "steps": steps, "warmup": warmup,
+      "statistic": "mean", "scaling": scaling,
+      "config": {"workload": workload, "M": M, "N": N_total, "K": K, "n_per_gpu": n, "cfg": cfg_name,
+                 "cfg_name": cfg.name, "kernel": info["kernel"], "grid": info["grid"], "smem": info["smem_bytes"],
+                 "parallelism": f"N-column shards x{self.world} (A replicated, no collective in the GEMM)",
+                 "l2": "flushed between steps (256 MiB write); each step timed alone with CUDA events"},
+      "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": peak, "unit": "TFLOP/s",
+                   "frac": round(achieved / peak, 4), "traffic": traffic,
+                   "peak_source": f"{self.peaks['source']} bf16_tflops (burst, cuBLAS 8192^3)",
+                   "algorithmic_flops_per_launch": flops_rank,
+                   "algorithmic_bytes_per_launch": 2 * (M * K + n * K + M * n)},
+      "cublas": {"value": round(flops_rank * self.world / (cmp["cublas_mean_ms"] * 1e-3) / 1e12, 3), "unit": "TFLOPS",
+                 "ours_over_cublas": round(cmp["cublas_mean_ms"] / cmp["ours_mean_ms"], 4), "statistic": "mean",
+                 "interleaved_steps": pair_steps, **{k: round(v, 5) for k, v in cmp.items()},
+                 "ours_over_cublas_median": round(cmp["cublas_median_ms"] / cmp["ours_median_ms"], 4),
+                 "clocks": clocks_pair.summary(),
+                 "kernel": "torch.matmul (cuBLAS), same inputs, same flush protocol, alternating with ours"},
+      "parity": parity, "clocks": clocks.summary(), "gpu_launches": steps,
+    }
+    if per_rank_clocks:
+      s = clocks.summary()
+      mine = [float(s.get("sm_mhz") or 0.0), float(sum(ClockSampler.REASONS[r] for r in s.get("reasons", []))),
+              float(s.get("samples", 0))]
+      res["clocks_per_rank"] = [
+        {"rank": r, "sm_mhz": v[0], "samples": int(v[2]),
+         "reasons": [k for k, bit in ClockSampler.REASONS.items() if int(v[1]) & bit]}
+        for r, v in enumerate(self.gather(mine))]
+    return res, launch, (A, BT, C, cfg, M, n, K)
+
+  def e2e(self, cfg, M, n, K, A, BT, C):
+    """End to end through the public API, as a caller streaming batches would run it: every step copies its A and
+    B from pinned host memory, runs the reference-facing operator build_gemm_ws(...)(A, B, C)() (plan and launch; B
+    is read as given for CTA-pair tiles, copied K-major first otherwise) and copies C back to pinned host memory.
+    Steps rotate over three streams and buffer sets (two when a set would exceed 1 GiB), so one step's host-to-device
+    copies overlap earlier steps' GEMMs and device-to-host copies without queueing behind them on a shared stream."""
+    torch = self.torch
+    from hopper_wgmma.gemm import build_gemm_ws
     sets = []
     nsets = 3 if 2 * (M * K + K * n + M * n) <= (1 << 30) else 2
-    for j in range(nsets):
+    for _ in range(nsets):
       hA = torch.empty((M, K), dtype=torch.bfloat16, pin_memory=True)
       hB = torch.empty((K, n), dtype=torch.bfloat16, pin_memory=True)
       hC = torch.empty((M, n), dtype=torch.bfloat16, pin_memory=True)
       hA.copy_(A.cpu())
       hB.copy_(BT.t().cpu())
-      dA, dB, dC = torch.empty_like(A), torch.empty((K, n), dtype=torch.bfloat16, device=dev), torch.empty_like(C)
-      sets.append((hA, hB, hC, dA, dB, dC, torch.cuda.Stream(device=dev)))
+      dA, dB, dC = torch.empty_like(A), torch.empty((K, n), dtype=torch.bfloat16, device=self.dev), torch.empty_like(C)
+      sets.append((hA, hB, hC, dA, dB, dC, torch.cuda.Stream(device=self.dev)))
     run = build_gemm_ws(n, cfg, M, K)
 
-    def e2e_step(i):
+    def step(i):
       hA, hB, hC, dA, dB, dC, st = sets[i % nsets]
       with torch.cuda.stream(st):
         dA.copy_(hA, non_blocking=True)
         dB.copy_(hB, non_blocking=True)
         run(dA, dB, dC)()
         hC.copy_(dC, non_blocking=True)
-    e2e_steps = max(3, min(args.steps, 30))
-    for i in range(2 * nsets): e2e_step(i)
+    steps = max(3, min(self.args.steps, 30))
+    for i in range(2 * nsets): step(i)
     torch.cuda.synchronize()
-    barrier()
-    cur = torch.cuda.current_stream(dev)
+    self.barrier()
+    cur = torch.cuda.current_stream(self.dev)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ev0.record(cur)
-    for _, _, _, _, _, _, st in sets: st.wait_event(ev0)
-    for i in range(e2e_steps): e2e_step(i)
-    for _, _, _, _, _, _, st in sets:
+    for *_, st in sets: st.wait_event(ev0)
+    for i in range(steps): step(i)
+    for *_, st in sets:
       done = torch.cuda.Event()
       done.record(st)
       cur.wait_event(done)
     ev1.record(cur)
     torch.cuda.synchronize()
-    barrier()
-    e2e_ms = ev0.elapsed_time(ev1)
-    if world > 1: e2e_ms = shard.max_over_ranks(e2e_ms, device=dev)
-    e2e = {"value": round(flops_rank * world / (e2e_ms / e2e_steps * 1e-3) / 1e12, 3), "unit": "TFLOPS",
-           "h2d_bytes_per_step": 2 * (M * K + K * n), "d2h_bytes_per_step": 2 * M * n,
-           "path": "pinned host A,B -> build_gemm_ws(...)(A, B, C)() ("
-                   f"{'B read N-major as given' if cfg.reads_b_directly else 'K-major copy of B'}, plan, launch) -> "
-                   f"pinned host C; {nsets} streams and buffer sets, steps overlapped",
-           "steps": e2e_steps, "ms_per_step": round(e2e_ms / e2e_steps, 4)}
+    self.barrier()
+    e2e_ms = self.max_over_ranks(ev0.elapsed_time(ev1))
+    flops_rank = 2.0 * M * n * K
+    return {"value": round(flops_rank * self.world / (e2e_ms / steps * 1e-3) / 1e12, 3), "unit": "TFLOPS",
+            "h2d_bytes_per_step": 2 * (M * K + K * n), "d2h_bytes_per_step": 2 * M * n,
+            "path": "pinned host A,B -> build_gemm_ws(...)(A, B, C)() ("
+                    f"{'B read N-major as given' if cfg.reads_b_directly else 'K-major copy of B'}, plan, launch) -> "
+                    f"pinned host C; {nsets} streams and buffer sets, steps overlapped",
+            "steps": steps, "ms_per_step": round(e2e_ms / steps, 4)}
 
-  # Optional NCCL all-gather of the C shards over NVLink (A replicated, B and C column-sharded): timed separately,
-  # never inside the GEMM. Every rank runs the same collectives in the same order.
-  allgather = None
-  if world > 1:
-    for _ in range(3): shard.gather_columns(C, world, as_row_major=False)
+  def allgather(self, C, M, n):
+    """Optional NCCL all-gather of the C shards over NVLink (A replicated, B and C column-sharded): timed
+    separately, never inside the GEMM. Every rank runs the same collectives in the same order."""
+    torch = self.torch
+    from hopper_wgmma import shard
+    for _ in range(3): shard.gather_columns(C, self.world, as_row_major=False)
     torch.cuda.synchronize()
-    barrier()
-    ag_steps = 10
+    self.barrier()
+    steps = 10
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ev0.record()
-    for _ in range(ag_steps): shard.gather_columns(C, world, as_row_major=False)
+    for _ in range(steps): shard.gather_columns(C, self.world, as_row_major=False)
     ev1.record()
     torch.cuda.synchronize()
-    ag_ms = shard.max_over_ranks(ev0.elapsed_time(ev1) / ag_steps, device=dev)
-    total_bytes = 2 * M * n * world
-    allgather = {"ms": round(ag_ms, 4), "bytes_gathered": total_bytes,
-                 "algbw_gbs": round(total_bytes / (ag_ms * 1e-3) / 1e9, 1),
-                 "busbw_gbs": round(total_bytes * (world - 1) / world / (ag_ms * 1e-3) / 1e9, 1),
-                 "what": "torch.distributed.all_gather_into_tensor (NCCL) of the bf16 C shards -> [world, M, N/world]"}
+    ms = self.max_over_ranks(ev0.elapsed_time(ev1) / steps)
+    total = 2 * M * n * self.world
+    return {"ms": round(ms, 4), "bytes_gathered": total, "algbw_gbs": round(total / (ms * 1e-3) / 1e9, 1),
+            "busbw_gbs": round(total * (self.world - 1) / self.world / (ms * 1e-3) / 1e9, 1),
+            "what": "torch.distributed.all_gather_into_tensor (NCCL) of the bf16 C shards -> [world, M, N/world]"}
+
+
+def run_ours(args) -> int:
+  b = Bench(args)
+  torch = b.torch
+  main, launch, (A, BT, C, cfg, M, n, K) = b.leg(args.workload, args.cfg, args.steps, args.warmup)
+  e2e = None if args.no_e2e else b.e2e(cfg, M, n, K, A, BT, C)
+  allgather = b.allgather(C, M, n) if b.world > 1 else None
+  del A, BT, C, launch
+  torch.cuda.empty_cache()
+
+  extra = {}
+  if not args.no_extra_legs:
+    leg_steps, leg_warmup = max(3, min(args.steps, EXTRA_LEG_STEPS)), max(3, min(args.warmup, 5))
+    legs = [("shard32k", True)] if b.world > 1 else [("gemm8192", False), ("shard32k", True)]
+    for wl, per_rank in legs:
+      if wl == args.workload: continue
+      res, *_ = b.leg(wl, "best", leg_steps, leg_warmup, per_rank_clocks=per_rank)
+      torch.cuda.empty_cache()
+      extra[wl] = res
 
   cpu = None
-  if rank == 0 and world == 1 and not args.no_cpu_baseline:
-    tf, reps, secs = cpu_gemm_tflops(2048, 2048, 2048, CPU_SAMPLE_SECONDS, reps_min=2)
+  if b.rank == 0 and b.world == 1 and not args.no_cpu_baseline:
+    tf, reps, secs = cpu_gemm_tflops(M, n, K, CPU_SAMPLE_SECONDS, reps_min=2)
     cpu = {"value": round(tf, 4), "unit": "TFLOPS", "cores": blas_threads(), "kind": "port",
-           "sample": f"{reps} x numpy fp32 GEMM 2048x2048x2048 + bf16 rounding in {secs:.1f} s"}
+           "sample": f"{reps} x numpy fp32 GEMM {M}x{n}x{K} + bf16 rounding in {secs:.1f} s (the arm's own shape)"}
 
-  if world > 1:
-    dist.barrier()
-    dist.destroy_process_group()
-  if rank != 0: return
-  tag = (f"sm100_gemm_ws_{'pair' if info['paired'] else 'cta'}_{'tmast' if cfg.tma_store else 'reg'}"
-         f"{'_x2' if cfg.n_mma == 2 else ''}")
-  traffic = profiled_traffic(tag, args.workload, flops_rank)
+  if b.world > 1:
+    b.dist.barrier()
+    b.dist.destroy_process_group()
   line = {
-    "metric": METRIC, "value": round(value, 3), "unit": "TFLOPS", "n_gpus": world, "steps": args.steps,
-    "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": True, "scaling": scaling,
+    "metric": METRIC, "value": main["value"], "unit": "TFLOPS", "n_gpus": b.world, "steps": args.steps,
+    "warmup": args.warmup, "ms_per_step": main["ms_per_step"], "higher_is_better": True, "scaling": main["scaling"],
     "vs_baseline": None, "dtype": "bf16", "data": "synthetic: seeded N(0,1) rounded to bf16, resident in HBM",
-    "config": {"workload": args.workload, "M": M, "N": N_total, "K": K, "n_per_gpu": n, "cfg": cfg_name,
-               "cfg_name": cfg.name, "kernel": info["kernel"], "grid": info["grid"], "smem": info["smem_bytes"],
-               "parallelism": f"N-column shards x{world} (A replicated, no collective in the GEMM)",
-               "l2": "flushed between steps (256 MiB write); each step timed alone with CUDA events"},
-    "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
-                 "frac": round(achieved / peaks["bf16_tflops"], 4), "traffic": traffic,
-                 "peak_source": f"{peaks['source']} bf16_tflops (burst, cuBLAS 8192^3)",
-                 "algorithmic_flops_per_launch": flops_rank},
-    "cublas": {"value": round(cub_tflops, 3), "unit": "TFLOPS", "ours_over_cublas": round(cub_med / ours_med, 4),
-               "interleaved_steps": pair_steps, "ours_median_ms": round(ours_med, 5), "cublas_median_ms": round(cub_med, 5),
-               "kernel": "torch.matmul (cuBLAS), same inputs, same flush protocol, alternating with ours"},
-    "parity": {"rel_err_vs_cublas": rel, "bitwise_equal_fraction_vs_cublas": round(equal, 4), "nan_after_poison": nan},
-    "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": args.steps, "clocks": clocks.summary(),
-    "allgather_c": allgather,
+    "statistic": "mean step time (CUDA events, L2 flushed before every step), max over ranks",
+    "config": main["config"], "roofline": main["roofline"], "cublas": main["cublas"], "parity": main["parity"],
+    "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": args.steps, "clocks": main["clocks"],
+    "allgather_c": allgather, **extra,
   }
-  emit(line)
+  bad = gates_failed(line)
+  if bad: line["parity_gate_failed"] = bad
+  if b.rank == 0: emit(line)
+  return GATE_FAILED_EXIT if bad else 0
 
 
 _JSON_OUT = None
@@ -420,9 +535,11 @@ def main():
   _JSON_OUT = os.fdopen(os.dup(1), "w")
   os.dup2(2, 1)
   args = parse_args()
-  if args.impl == "reference": run_reference(args)
-  else: run_ours(args)
+  if args.impl == "reference":
+    run_reference(args)
+    return 0
+  return run_ours(args)
 
 
 if __name__ == "__main__":
-  main()
+  sys.exit(main())

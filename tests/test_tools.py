@@ -104,3 +104,55 @@ def test_bench_reads_traffic_lines_of_the_committed_profiles():
   assert t is not None and 67_108_864 <= t <= 2 * 101_000_000      # at least the compulsory A + B
   assert bench.profiled_traffic("sm100_gemm_ws_pair_tmast_x2", "gemm8192", 2.0 * 8192 ** 3) is not None
   assert bench.profiled_traffic("no_such_kernel", "gemm4096", flops) is None
+
+
+def test_bench_parity_gate_fails_on_a_planted_error_or_nan():
+  """The bench's correctness gate compares the bf16 output with the fp32 product; an output with one wrong element
+  (planted here on the CPU) or one surviving NaN must fail it."""
+  import torch
+  sys.path.insert(0, str(ROOT))
+  import bench
+  g = torch.Generator().manual_seed(0)
+  ref = torch.randn((64, 96), generator=g) * 10
+  C = ref.to(torch.bfloat16)
+  assert bench.parity_gate(C, ref)["ok"]
+  bad = C.clone()
+  bad[3, 7] += 1.0
+  res = bench.parity_gate(bad, ref)
+  assert not res["ok"] and res["rel_err_vs_fp32"] > bench.TOL
+  bad = C.clone()
+  bad[5, 5] = float("nan")
+  res = bench.parity_gate(bad, ref)
+  assert not res["ok"] and res["nan_after_poison"] == 1
+
+
+def test_bench_exits_nonzero_when_a_leg_misses_the_gate(monkeypatch):
+  """run_ours still prints its line but returns the failure status when any leg's gate failed."""
+  sys.path.insert(0, str(ROOT))
+  import bench
+  from hopper_wgmma import WSCfg
+
+  class FakeTorch:
+    class cuda:
+      @staticmethod
+      def empty_cache(): pass
+
+  class FakeBench:
+    def __init__(self, args):
+      self.torch, self.world, self.rank = FakeTorch, 1, 0
+
+    def leg(self, workload, cfg_name, steps, warmup, per_rank_clocks=False):
+      ok = workload != "gemm8192"                  # the planted failure: one extra leg misses the gate
+      res = {"value": 1.0, "ms_per_step": 1.0, "scaling": "weak", "config": {}, "roofline": {}, "cublas": {},
+             "parity": {"ok": ok}, "clocks": {}}
+      return res, None, (None, None, None, WSCfg(), 64, 64, 64)
+
+  printed = []
+  monkeypatch.setattr(bench, "Bench", FakeBench)
+  monkeypatch.setattr(bench, "emit", printed.append)
+  args = bench.parse_args(["--no-e2e", "--no-cpu-baseline"])
+  assert bench.run_ours(args) == bench.GATE_FAILED_EXIT
+  assert printed and printed[0]["parity_gate_failed"] == ["gemm8192"]
+  args = bench.parse_args(["--no-e2e", "--no-cpu-baseline", "--no-extra-legs"])
+  printed.clear()
+  assert bench.run_ours(args) == 0 and "parity_gate_failed" not in printed[0]
