@@ -373,7 +373,9 @@ class Bench:
       cmp = self.interleaved(launch, cub, pair_steps)
     del Cc
     peak = self.peaks["bf16_tflops"]
-    traffic = profiled_traffic(kernel_tag(info, cfg), workload, flops_rank)
+    # strong scaling changes the per-rank shape with the world size: its captures are keyed "shard32k/<world>"
+    traffic = profiled_traffic(kernel_tag(info, cfg), workload if scaling == "weak" else f"{workload}/{self.world}",
+                               flops_rank)
     res = {
       "value": round(value, 3), "unit": "TFLOPS", "ms_per_step": round(ms, 5), "steps": steps, "warmup": warmup,
       "statistic": "mean", "scaling": scaling,

@@ -37,7 +37,8 @@ enum {
   BG_ERR_EPILOGUE = 4,   /* epilogue timed out waiting for a finished accumulator */
   BG_ERR_DRAIN = 5,      /* final wait for outstanding MMAs timed out             */
   BG_ERR_LOAD_DRAIN = 6, /* wait for in-flight loads after another error timed out */
-  BG_ERR_SPLIT_K = 7     /* split-K (one wave): a tile's other splits did not all publish in time */
+  BG_ERR_SPLIT_K = 7,    /* split-K (one wave): a tile's other splits did not all publish in time */
+  BG_ERR_WAVE_SYNC = 8   /* wave barrier: the other CTAs did not all reach a tile boundary in time */
 };
 
 /*
@@ -81,6 +82,11 @@ enum {
  *               tcgen05 descriptors, so the caller makes no transposed copy. Needs each CTA's share of a tile's
  *               columns (BN, or BN / 2 in a CTA pair) to be a multiple of 64; half-width tail tiles are used only
  *               when their share is too.
+ *   wave_sync   0 (default): automatic — on for persistent schedules without split-K that give each cluster at
+ *               least 8 tiles, off otherwise; 1: on (persistent kernel, no split-K); 2: off. When on, the TMA
+ *               producers of all CTAs meet at every tile boundary (a bounded wait on a plan-owned 64-bit counter),
+ *               so the tiles of one wave stay in step and share their operand panels through L2; without it CTAs
+ *               drift apart over many tiles and re-read the panels from DRAM. Not used by bg_gemm_noalloc.
  */
 typedef struct bg_cfg {
   int32_t kind;
@@ -103,6 +109,7 @@ typedef struct bg_cfg {
   int32_t split_k;
   int32_t no_k_serpentine;
   int32_t b_nmajor;
+  int32_t wave_sync;
 } bg_cfg;
 
 /* What a plan resolved to (for reports and tests). */

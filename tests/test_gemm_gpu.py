@@ -480,3 +480,73 @@ def test_plan_tables_hold_bounded_device_memory(cuda_dev):
   assert free_warm - free_after < (24 << 20), (free_warm, free_after)
   worst, _ = run_case(small, 512, 512, 320, cuda_dev, reps=1)
   assert worst <= TOL
+
+
+# ------------------------------------------------------------------------------------------------------------------
+# wave barrier (WSCfg(wave_sync=True)): the producers of all CTAs meet at every tile boundary
+# ------------------------------------------------------------------------------------------------------------------
+def _wave_sync_cases():
+  from hopper_wgmma import WSCfg
+  return [
+    ("pair_hilbert_8_waves", WSCfg(tma_store=True, cluster=2, hilbert=True, num_sm=8, wave_sync=True), (1024, 2048, 256)),
+    ("pair_ragged_deal", WSCfg(tma_store=True, cluster=2, hilbert=True, num_sm=14, wave_sync=True), (1280, 1536, 192)),
+    ("cta_tail_split", WSCfg(BN=128, tma_store=True, num_sm=6, wave_sync=True), (512, 640, 192)),
+    ("wide_pair_waves", WSCfg(n_mma=2, cluster=2, tma_store=True, num_sm=10, wave_sync=True), (1024, 2048, 640)),
+    ("regstore_bm64", WSCfg(consumers=1, BN=128, num_sm=7, wave_sync=True), (320, 384, 128)),
+  ]
+
+
+@pytest.mark.parametrize("idx", range(5))
+def test_wave_sync(idx, cuda_dev):
+  """Three launches of one plan: the barrier's counter keeps counting across launches (each launch starts from
+  where the previous one left it)."""
+  from hopper_wgmma import build_gemm_ws
+  name, cfg, (M, N, K) = _wave_sync_cases()[idx]
+  worst, launch = run_case(lambda: build_gemm_ws(N, cfg, M, K, wait_budget_ns=BUDGET_NS), M, N, K, cuda_dev)
+  assert "wavesync" in launch.info()["kernel"], launch.info()["kernel"]
+  assert worst <= TOL, f"{name} {M}x{N}x{K}: relative_error={worst:.5f} ({launch.info()['kernel']})"
+
+
+def test_wave_sync_many_launches_and_auto_choice(cuda_dev):
+  """Fifty launches back to back with one check at the end; the automatic choice turns the barrier on at 8 tiles
+  per cluster and leaves shorter schedules alone."""
+  torch = _torch()
+  from hopper_wgmma import WSCfg, build_gemm_ws
+  from oracle import gemm_ref
+  M, N, K = 1024, 2048, 128
+  a_bits, b_bits = inputs(M, N, K, seed=8)
+  A, B = to_dev(a_bits, cuda_dev), to_dev(b_bits, cuda_dev)
+  C = torch.empty((M, N), dtype=torch.bfloat16, device=cuda_dev)
+  launch = build_gemm_ws(N, WSCfg(tma_store=True, cluster=2, hilbert=True, num_sm=8), M, K,
+                         wait_budget_ns=BUDGET_NS)(A, B, C)              # 32 tiles on 4 clusters: 8 each
+  assert "wavesync" in launch.info()["kernel"]
+  poison(C)
+  for _ in range(50): launch()
+  launch.check()
+  assert gemm_ref.rel_err(to_bits(C), gemm_ref.gemm_f32(a_bits, b_bits)) <= TOL
+  short = build_gemm_ws(N, WSCfg(tma_store=True, cluster=2, hilbert=True, num_sm=10), M, K)(A, B, C)   # 6.4 each
+  assert "wavesync" not in short.info()["kernel"]
+
+
+def test_wave_sync_timeout_reports_error_and_recovers(cuda_dev):
+  """A stage the producer never loads in a plan with the wave barrier: the launch's bounded waits run out, the launch
+  reports the error (and the check resets the plan's wave counter), and the GPU then runs wave-barrier plans
+  correctly, twice in a row."""
+  torch = _torch()
+  from hopper_wgmma import WSCfg, build_gemm_ws
+  from oracle import gemm_ref
+  cfg = WSCfg(BN=128, tma_store=True, num_sm=4, wave_sync=True)
+  M, N, K = 512, 512, 128                                               # 16 tiles on 4 CTAs
+  a_bits, b_bits = inputs(M, N, K, seed=9)
+  A, B = to_dev(a_bits, cuda_dev), to_dev(b_bits, cuda_dev)
+  C = torch.empty((M, N), dtype=torch.bfloat16, device=cuda_dev)
+  bad = build_gemm_ws(N, cfg, M, K, wait_budget_ns=50_000_000, debug_skip_job=1)(A, B, C)
+  bad()
+  with pytest.raises(RuntimeError, match="timed out"):
+    bad.check()
+  good = build_gemm_ws(N, cfg, M, K, wait_budget_ns=BUDGET_NS)(A, B, C)
+  for _ in range(2):
+    poison(C)
+    good()
+    good.check()
+    assert gemm_ref.rel_err(to_bits(C), gemm_ref.gemm_f32(a_bits, b_bits)) <= TOL

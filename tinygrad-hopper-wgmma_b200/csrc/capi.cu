@@ -204,6 +204,9 @@ struct bg_plan {
   bool holds_table = false;          // d_sched is a reference on the device store's table table_key
   std::array<int, 8> table_key{};
   unsigned int* d_err = nullptr;
+  unsigned long long* d_wave = nullptr;   // wave-barrier counter (from the device store's slab), or null
+  unsigned long long wave_per_launch = 0; // arrivals one launch adds to it
+  unsigned long long launches = 0;        // launches enqueued since the counter was last zero
   size_t partial_bytes = 0;          // split-K workspace, owned by the plan
   size_t ticket_words = 0;
   float* d_partial = nullptr;
@@ -254,6 +257,7 @@ struct DeviceStore {
   std::map<std::array<int, 8>, TableEntry> tables;
   uint64_t clock = 0;
   std::vector<unsigned int*> free_words;
+  std::vector<unsigned long long*> free_counters;
 };
 
 DeviceStore& device_store(int dev) {
@@ -338,6 +342,25 @@ int32_t take_error_word(int dev, unsigned int** out) {
   return 0;
 }
 
+// A zeroed 64-bit counter (the wave barrier's), handed out from 4 KiB slabs like the error words.
+int32_t take_counter(int dev, unsigned long long** out) {
+  DeviceStore& s = device_store(dev);
+  std::lock_guard<std::mutex> lock(s.mu);
+  if (s.free_counters.empty()) {
+    constexpr int kCounters = 512;
+    unsigned long long* slab = nullptr;
+    cudaError_t e = cudaMalloc(&slab, kCounters * sizeof(unsigned long long));
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(wave counters)");
+    for (int i = kCounters - 1; i >= 0; --i) s.free_counters.push_back(slab + i);
+  }
+  unsigned long long* c = s.free_counters.back();
+  cudaError_t e = cudaMemset(c, 0, sizeof(unsigned long long));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemset(wave counter)");
+  s.free_counters.pop_back();
+  *out = c;
+  return 0;
+}
+
 void free_plan(bg_plan* p) {
   if (p == nullptr) return;
   if (p->d_partial || p->d_tickets || p->holds_table) {
@@ -346,10 +369,11 @@ void free_plan(bg_plan* p) {
     if (p->d_tickets) cudaFree(p->d_tickets);
     if (p->holds_table) release_table(p->device, p->table_key);
   }
-  if (p->d_err) {
+  if (p->d_err || p->d_wave) {
     DeviceStore& s = device_store(p->device);
     std::lock_guard<std::mutex> lock(s.mu);
-    s.free_words.push_back(p->d_err);
+    if (p->d_err) s.free_words.push_back(p->d_err);
+    if (p->d_wave) s.free_counters.push_back(p->d_wave);
   }
   delete p;
 }
@@ -456,6 +480,9 @@ int32_t setup_plan(const bg_cfg& c, int64_t M, int64_t N, int64_t K, const void*
   const bool nmajor = c.b_nmajor != 0;
   if (c.b_nmajor != 0 && c.b_nmajor != 1) return fail(-1, "b_nmajor must be 0 or 1");
   if (nmajor && c.kind != BG_KIND_WS) return fail(-1, "b_nmajor needs the warp-specialized kernel");
+  if (c.wave_sync < 0 || c.wave_sync > 2) return fail(-1, "wave_sync must be 0 (auto), 1 (on) or 2 (off)");
+  if (c.wave_sync == 1 && (c.kind != BG_KIND_WS || sk > 1))
+    return fail(-1, "wave_sync needs the persistent kernel without split-K");
 
   const int bm = 64 * std::max(c.consumers, 1);
   const int cl = c.cluster;
@@ -674,6 +701,18 @@ int32_t setup_plan(const bg_cfg& c, int64_t M, int64_t N, int64_t K, const void*
     p->tmC = p->tmA;   // unused by the register epilogue
   }
 
+  // ---- wave barrier: on request, or automatically once each cluster runs kAutoWaveSyncTiles tiles or more (the
+  // drift it removes grows with the tiles per cluster; below that the barrier's waits would cost more than it saves)
+  constexpr int64_t kAutoWaveSyncTiles = 8;
+  const bool wave_ok = c.kind == BG_KIND_WS && sk == 1 && n_entries > nclusters;
+  const bool wave = wave_ok && (c.wave_sync == 1 || (c.wave_sync == 0 && n_entries >= kAutoWaveSyncTiles * nclusters));
+  p->wave_per_launch = 0;
+  if (wave) {
+    for (int64_t j = 1; j * nclusters < n_entries; ++j)
+      p->wave_per_launch += static_cast<unsigned long long>(std::min<int64_t>(nclusters, n_entries - j * nclusters)) *
+                            static_cast<unsigned long long>(cl);
+  }
+
   GemmParams& kp = p->kp;
   kp.num_kb = static_cast<int>(nkb);
   kp.bn = bn;
@@ -709,6 +748,9 @@ int32_t setup_plan(const bg_cfg& c, int64_t M, int64_t N, int64_t K, const void*
   kp.sk_scatter = sk_scatter ? 1 : 0;
   kp.k_serpentine = c.no_k_serpentine ? 0 : 1;
   kp.b_nmajor = nmajor ? 1 : 0;
+  kp.wave_sync = wave ? 1 : 0;
+  kp.wave_ctr = nullptr;
+  kp.wave_base = 0;
   // A cooperative launch guarantees that every CTA is resident at once. It cannot be combined with cluster
   // dimensions here (such a launch fails under Nsight Compute), so CTA pairs rely on the persistent grid being
   // capped at what the GPU co-schedules, with the bounded wait reporting an error if other work holds SMs.
@@ -719,10 +761,10 @@ int32_t setup_plan(const bg_cfg& c, int64_t M, int64_t N, int64_t K, const void*
   // the first wave of the tile table also travels in the kernel parameters (see FirstTile in the kernel)
   for (size_t i = 0; i < sched.size() && i < static_cast<size_t>(sm100::kFirstWave); ++i) kp.first_wave[i] = sched[i];
 
-  snprintf(p->name, sizeof(p->name), "%s<BM=%d,%s,%s> BN=%dx%d stages=%d acc=%d tail=%d splitk=%d b=%s",
+  snprintf(p->name, sizeof(p->name), "%s<BM=%d,%s,%s> BN=%dx%d stages=%d acc=%d tail=%d splitk=%d%s b=%s",
            c.kind == BG_KIND_RING ? "sm100_gemm_ring" : "sm100_gemm_ws", bm,
            paired ? "pair" : (cl == 2 ? "cluster2" : "cta"), p->tma_store ? "tma_store" : "reg_store", bn, nblk,
-           stages, acc_bufs, p->narrow_tiles, sk, nmajor ? "N" : "K");
+           stages, acc_bufs, p->narrow_tiles, sk, wave ? " wavesync" : "", nmajor ? "N" : "K");
   return 0;
 }
 
@@ -750,6 +792,7 @@ int32_t bg_plan_create(bg_plan** out, const bg_cfg* cfg, int64_t M, int64_t N, i
     p->table_key = sched_key;
   }
   if ((st = take_error_word(device, &p->d_err))) return st;
+  if (p->kp.wave_sync && (st = take_counter(device, &p->d_wave))) return st;
   if (p->partial_bytes > 0) {
     // split-K workspace: partial sums (fully written before they are read) and zeroed arrival words
     cudaError_t e = cudaMalloc(&p->d_partial, p->partial_bytes);
@@ -761,6 +804,7 @@ int32_t bg_plan_create(bg_plan** out, const bg_cfg* cfg, int64_t M, int64_t N, i
   }
   p->kp.sched = p->d_sched;
   p->kp.err = p->d_err;
+  p->kp.wave_ctr = p->d_wave;
   p->kp.partial = p->d_partial;
   p->kp.tickets = p->d_tickets;
   *out = p.release();
@@ -810,6 +854,7 @@ int32_t bg_gemm_noalloc(const bg_cfg* cfg, int64_t M, int64_t N, int64_t K, cons
   // workspace this entry point does not have: here those shapes run unsplit.
   bg_cfg c = *cfg;
   if (c.split_k == -1) c.split_k = 1;
+  c.wave_sync = 2;   // the wave barrier needs a counter this entry point does not have
   bg_plan plan;   // lives on this stack frame and owns no device memory
   std::vector<int32_t> sched;
   std::array<int, 8> sched_key{};
@@ -883,12 +928,15 @@ int32_t bg_plan_launch(bg_plan* p, void* stream) {
     at[lc.numAttrs].val.cooperative = 1;
     ++lc.numAttrs;
   }
+  // the wave barrier's counter keeps counting across launches: this launch starts where the previous ones left it
+  if (p->kp.wave_sync) p->kp.wave_base = p->launches * p->wave_per_launch;
   cudaError_t e;
   if (p->kind == BG_KIND_RING)
     e = cudaLaunchKernelEx(&lc, p->ring, p->tmA, p->tmB, p->kp);
   else
     e = cudaLaunchKernelEx(&lc, p->ws, p->tmA, p->tmB, p->tmBn, p->tmC, p->kp);
   if (e != cudaSuccess) return cuda_fail(e, "cudaLaunchKernelEx");
+  ++p->launches;
   return 0;
 }
 
@@ -906,11 +954,17 @@ int32_t bg_plan_check_error(bg_plan* p, void* stream, uint32_t* err_word) {
     cudaMemset(p->d_err, 0, sizeof(uint32_t));
     // an interrupted split-K launch can leave arrival words behind; the next launch needs them zero
     if (p->d_tickets) cudaMemset(p->d_tickets, 0, p->ticket_words * sizeof(unsigned int));
+    // an interrupted launch leaves the wave barrier's count short: start counting afresh
+    if (p->d_wave) {
+      cudaMemset(p->d_wave, 0, sizeof(unsigned long long));
+      p->launches = 0;
+    }
     static const char* roles[] = {"?", "producer (free stage)", "MMA (loaded stage)", "MMA (free accumulator)",
                                   "epilogue (finished accumulator)", "MMA drain", "load drain",
-                                  "split-K (partial sums of the tile's other splits)"};
+                                  "split-K (partial sums of the tile's other splits)",
+                                  "wave barrier (other CTAs at a tile boundary)"};
     const uint32_t role = w >> 24;
-    return fail(6, "device wait timed out: %s, counter %u (error word 0x%08x)", role < 8 ? roles[role] : "?",
+    return fail(6, "device wait timed out: %s, counter %u (error word 0x%08x)", role < 9 ? roles[role] : "?",
                 w & 0xFFFFFFu, w);
   }
   return 0;

@@ -54,6 +54,7 @@ enum : uint32_t {
   kErrDrain = 5u << 24,       // final wait for outstanding MMAs timed out
   kErrLoadDrain = 6u << 24,   // producer's final wait for its in-flight loads timed out (after another error)
   kErrSplitK = 7u << 24,      // split-K (one wave): the other entries of a tile did not all publish in time
+  kErrWaveSync = 8u << 24,    // wave barrier: the other CTAs did not all reach the tile boundary in time
 };
 
 struct GemmParams {
@@ -95,6 +96,9 @@ struct GemmParams {
   int sk_scatter;          // split-K with one entry per cluster, launched cooperatively: the reduce is shared out
   int k_serpentine;        // a cluster walks K backwards on its odd-numbered tiles (1) or always forwards (0)
   int b_nmajor;            // B is given as B[K,N] row-major (1; tmB/tmBn map it with 64 x 64 boxes) or as BT[N,K] (0)
+  int wave_sync;           // 1: the producers of all CTAs meet at every tile boundary (see wave_barrier)
+  unsigned long long* wave_ctr;   // wave barrier: arrivals, counted across launches (the plan's counter)
+  unsigned long long wave_base;   // wave barrier: the counter's value when this launch starts
   int32_t first_wave[kFirstWave];  // sched[0 .. min(tiles, kFirstWave)) again, delivered with the launch
 };
 
@@ -114,6 +118,38 @@ __device__ __forceinline__ void k_range(const GemmParams& p, int idx, int& kb0, 
 
 __device__ __forceinline__ void record_error(unsigned int* err, uint32_t role, uint32_t counter) {
   atomicCAS(err, 0u, role | (counter > 0xFFFFFFu ? 0xFFFFFFu : counter));
+}
+
+// Wave barrier (p.wave_sync): before loading its i-th tile (i >= 1), each CTA's producer counts itself on a
+// GPU-wide counter and waits until every CTA that has an i-th tile has done the same. Without it, CTAs drift apart
+// over many tiles (a few percent of speed accumulates to whole tiles), so the tiles of one wave that share an A or B
+// panel no longer read its K-slabs at about the same time, and L2 no longer serves the later readers: at 32768^3 on
+// one GPU (110 tiles per cluster) DRAM read 51x the compulsory bytes. The barrier keeps a wave's tiles within the
+// last tile's spread of each other. It publishes no data (relaxed counting); the wait is bounded. The counter counts
+// across launches: launch L starts at p.wave_base = L x (arrivals per launch), set by the host.
+__device__ __forceinline__ bool wave_barrier(const GemmParams& p, int i, uint64_t budget, int lane) {
+  bool ok = true;
+  if (lane == 0) {
+    // arrivals at boundaries 1..i: every CTA of each cluster that has a j-th tile
+    unsigned long long target = p.wave_base;
+    for (int j = 1; j <= i; ++j) {
+      const int left = p.tiles - j * p.nclusters;
+      target += static_cast<unsigned long long>(left < p.nclusters ? left : p.nclusters) * p.cl;
+    }
+    atomicAdd(p.wave_ctr, 1ull);
+    if (ld_relaxed_gpu_u64(p.wave_ctr) < target) {
+      const uint64_t t0 = globaltimer_ns();
+      while (ld_relaxed_gpu_u64(p.wave_ctr) < target) {
+        if (globaltimer_ns() - t0 > budget) {
+          ok = false;
+          break;
+        }
+        __nanosleep(64);
+      }
+    }
+  }
+  ok = __shfl_sync(0xffffffffu, ok ? 1u : 0u, 0) != 0;
+  return ok;
 }
 
 constexpr int kNarrowTile = 0x8000;   // column-field flag of a half-width tile (the last wave's split tiles)
@@ -272,6 +308,10 @@ __global__ void __launch_bounds__(kWsThreads, 1)
     for (int i = 0; !failed; ++i) {
       const int idx = cid + i * p.nclusters;
       if (idx >= p.tiles) break;
+      if (p.wave_sync && i > 0 && !wave_barrier(p, i, budget, lane)) {
+        if (lane == 0) record_error(p.err, kErrWaveSync, i);
+        break;
+      }
       int cm, tn;
       bool narrow;
       first.coords(p, idx, cm, tn, narrow);

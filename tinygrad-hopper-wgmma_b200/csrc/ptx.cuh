@@ -190,6 +190,13 @@ __device__ __forceinline__ uint32_t ld_acquire_gpu(const unsigned int* ptr) {
   return v;
 }
 
+// gpu-scope relaxed load of a 64-bit counter (a timing barrier: it orders no data).
+__device__ __forceinline__ unsigned long long ld_relaxed_gpu_u64(const unsigned long long* ptr) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(ptr) : "memory");
+  return v;
+}
+
 __device__ __forceinline__ void cp_async_16(uint32_t smem_dst, const void* gmem_src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_dst), "l"(gmem_src) : "memory");
 }

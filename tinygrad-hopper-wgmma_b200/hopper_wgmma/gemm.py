@@ -161,6 +161,9 @@ class WSCfg:
   b_nmajor: bool | None = None # build_gemm_ws reads B[K,N] as given (MN-major tcgen05 operand) instead of making
                                # the K-major copy BT (gemm.py:382): True = wherever the tile allows it, False = never,
                                # None = for CTA-pair tiles only (see reads_b_directly)
+  wave_sync: bool | None = None  # the TMA producers of all CTAs meet at every tile boundary, keeping a wave's tiles
+                               # in step so that they share operand panels through L2: True = on, False = off,
+                               # None = on for schedules of at least 8 tiles per cluster (no split-K)
 
   def __post_init__(self):
     if self.BK != 64: raise ValueError("BK must be 64 (one 128-byte swizzle atom)")
@@ -177,6 +180,7 @@ class WSCfg:
     if self.split_k != -1 and not 1 <= self.split_k <= 64: raise ValueError("split_k must be -1 (auto) or in [1, 64]")
     if self.split_k > 1 and self.width % 32: raise ValueError("split_k needs tiles a multiple of 32 columns wide")
     if self.acc_bufs is not None and self.acc_bufs not in (1, 2): raise ValueError("acc_bufs must be 1 or 2")
+    if self.wave_sync and self.split_k > 1: raise ValueError("wave_sync needs split_k = 1")
     if self.acc_bufs == 2 and 2 * self.width > 512: raise ValueError("two accumulators of the tile width exceed tensor memory")
     if self.stages_used < 2: raise ValueError(f"not even 2 stages fit in {SMEM_LIMIT} bytes of shared memory")
     if self.smem_bytes > SMEM_LIMIT: raise ValueError(f"needs {self.smem_bytes} bytes of shared memory, the limit is {SMEM_LIMIT}")
@@ -224,7 +228,8 @@ class WSCfg:
             f"{'_tmast' if self.tma_store else ''}{'_hil' if self.hilbert else ''}"
             f"{f'_r{self.regs[0]}x{self.regs[1]}' if self.regs else ''}{f'_cl{self.cluster}' if self.cluster > 1 else ''}"
             f"{f'_x{self.n_mma}' if self.n_mma > 1 else ''}{f'_sk{self.split_k}' if self.split_k > 1 else '_skA' if self.split_k == -1 else ''}"
-            f"{'' if self.k_serpentine else '_kfwd'}{'' if self.b_nmajor is None else '_bN' if self.b_nmajor else '_bT'}")
+            f"{'' if self.k_serpentine else '_kfwd'}{'' if self.b_nmajor is None else '_bN' if self.b_nmajor else '_bT'}"
+            f"{'' if self.wave_sync is None else '_wsync' if self.wave_sync else '_nowsync'}")
 
   def to_c(self, kind: int = _capi.KIND_WS, num_sm: int | None = None, wait_budget_ns: int = 0,
            debug_skip_job: int = -1, b_nmajor: bool = False) -> _capi.BgCfg:
@@ -235,7 +240,7 @@ class WSCfg:
                        acc_bufs=self.acc_bufs or 0, wait_budget_ns=wait_budget_ns, debug_skip_job=debug_skip_job,
                        n_mma=self.n_mma, no_tail_split=0 if self.split_tail else 1, ragged=int(self.ragged),
                        split_k=self.split_k, no_k_serpentine=0 if self.k_serpentine else 1,
-                       b_nmajor=int(b_nmajor))
+                       b_nmajor=int(b_nmajor), wave_sync={None: 0, True: 1, False: 2}[self.wave_sync])
 
 
 # =============================================================================================================

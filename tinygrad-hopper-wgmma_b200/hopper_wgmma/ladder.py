@@ -66,9 +66,11 @@ def lookup(name: str):
   """A config by name from LADDER, SWEEP, B200 or EXTRA, with optional ``@`` modifiers so that sweeps can vary one
   knob on any tile shape: ``@sk<S>`` sets ``split_k=S`` (``@skA`` = automatic), ``@reg`` selects the register
   epilogue (``tma_store=False``), ``@s<N>`` sets the ring depth ``stages=N``, ``@bT`` makes build_gemm_ws copy B
-  to a K-major BT first (``b_nmajor=False``, the reference's operand layout) and ``@bN`` makes it read B[K,N]
-  directly wherever the tile allows (``b_nmajor=True``). Example: ``cta_n128@sk2``, ``cta_n64@reg@skA``,
-  ``pair_n128@s4``, ``cluster_hilbert@bT``, ``cta_n128@bN``."""
+  to a K-major BT first (``b_nmajor=False``, the reference's operand layout), ``@bN`` makes it read B[K,N]
+  directly wherever the tile allows (``b_nmajor=True``) and ``@g<M>x<N>`` replaces the tile order by the grouped
+  order with ``group_m=M, group_n=N`` (``hilbert=False``); ``@wsync`` / ``@nowsync`` force the wave barrier
+  on or off (``wave_sync``). Example: ``cta_n128@sk2``, ``cta_n64@reg@skA``,
+  ``pair_n128@s4``, ``cluster_hilbert@bT``, ``cta_n128@bN``, ``pair_wide@g64x8``."""
   import dataclasses
   base, *mods = name.split("@")
   cfg = {**LADDER, **SWEEP, **EXTRA, **B200}[base]
@@ -80,6 +82,11 @@ def lookup(name: str):
       cfg = dataclasses.replace(cfg, split_k=-1 if mod[2:] == "A" else int(mod[2:]))
     elif mod in ("bT", "bN"):
       cfg = dataclasses.replace(cfg, b_nmajor=mod == "bN")
+    elif mod in ("wsync", "nowsync"):
+      cfg = dataclasses.replace(cfg, wave_sync=mod == "wsync")
+    elif mod.startswith("g") and "x" in mod and all(p.isdigit() for p in mod[1:].split("x", 1)):
+      gm, gn = (int(p) for p in mod[1:].split("x", 1))
+      cfg = dataclasses.replace(cfg, group_m=gm, group_n=gn, hilbert=False)
     elif mod.startswith("s") and mod[1:].isdigit():
       cfg = dataclasses.replace(cfg, stages=int(mod[1:]))
     else:
