@@ -83,7 +83,9 @@ enum {
  *               columns (BN, or BN / 2 in a CTA pair) to be a multiple of 64; half-width tail tiles are used only
  *               when their share is too.
  *   wave_sync   0 (default): automatic — on for persistent schedules without split-K that give each cluster at
- *               least 8 tiles, off otherwise; 1: on (persistent kernel, no split-K); 2: off. When on, the TMA
+ *               least 4 tiles and whose waves touch operand panels too big to stay in L2 (at least 96 MB by the
+ *               estimate 4 K sqrt(clusters x tile rows x tile columns) bytes: 256x512 pair tiles from K = 8192),
+ *               off otherwise; 1: on (persistent kernel, no split-K); 2: off. When on, the TMA
  *               producers of all CTAs meet at every tile boundary (a bounded wait on a plan-owned 64-bit counter),
  *               so the tiles of one wave stay in step and share their operand panels through L2; without it CTAs
  *               drift apart over many tiles and re-read the panels from DRAM. Not used by bg_gemm_noalloc.

@@ -508,24 +508,31 @@ def test_wave_sync(idx, cuda_dev):
 
 
 def test_wave_sync_many_launches_and_auto_choice(cuda_dev):
-  """Fifty launches back to back with one check at the end; the automatic choice turns the barrier on at 8 tiles
-  per cluster and leaves shorter schedules alone."""
+  """Fifty launches back to back with one check at the end. The automatic choice turns the barrier on where a wave's
+  operand panels outgrow L2 and each cluster runs several tiles (256x512 pair tiles at 8192^3), and leaves it off
+  for short K (4096^3 with 256x256 pair tiles, 6144^3 with 256x512)."""
   torch = _torch()
   from hopper_wgmma import WSCfg, build_gemm_ws
+  from hopper_wgmma.gemm import plan_gemm_bt
+  from hopper_wgmma.ladder import LADDER, best_config
   from oracle import gemm_ref
   M, N, K = 1024, 2048, 128
   a_bits, b_bits = inputs(M, N, K, seed=8)
   A, B = to_dev(a_bits, cuda_dev), to_dev(b_bits, cuda_dev)
   C = torch.empty((M, N), dtype=torch.bfloat16, device=cuda_dev)
-  launch = build_gemm_ws(N, WSCfg(tma_store=True, cluster=2, hilbert=True, num_sm=8), M, K,
+  launch = build_gemm_ws(N, WSCfg(tma_store=True, cluster=2, hilbert=True, num_sm=8, wave_sync=True), M, K,
                          wait_budget_ns=BUDGET_NS)(A, B, C)              # 32 tiles on 4 clusters: 8 each
   assert "wavesync" in launch.info()["kernel"]
   poison(C)
   for _ in range(50): launch()
   launch.check()
   assert gemm_ref.rel_err(to_bits(C), gemm_ref.gemm_f32(a_bits, b_bits)) <= TOL
-  short = build_gemm_ws(N, WSCfg(tma_store=True, cluster=2, hilbert=True, num_sm=10), M, K)(A, B, C)   # 6.4 each
-  assert "wavesync" not in short.info()["kernel"]
+  for size, cfg, on in ((8192, best_config(8192, 8192, 8192), True), (6144, best_config(6144, 6144, 6144), False),
+                        (4096, LADDER["cluster_hilbert"], False)):
+    X = torch.empty((size, size), dtype=torch.bfloat16, device=cuda_dev)
+    plan = plan_gemm_bt(X, X, X, cfg)                                    # planned only, never launched
+    assert ("wavesync" in plan.info()["kernel"]) == on, (size, plan.info()["kernel"])
+    del plan, X
 
 
 def test_wave_sync_timeout_reports_error_and_recovers(cuda_dev):

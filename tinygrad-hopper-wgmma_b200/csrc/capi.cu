@@ -10,6 +10,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <cmath>
 #include <array>
 #include <map>
 #include <cstdarg>
@@ -701,11 +702,21 @@ int32_t setup_plan(const bg_cfg& c, int64_t M, int64_t N, int64_t K, const void*
     p->tmC = p->tmA;   // unused by the register epilogue
   }
 
-  // ---- wave barrier: on request, or automatically once each cluster runs kAutoWaveSyncTiles tiles or more (the
-  // drift it removes grows with the tiles per cluster; below that the barrier's waits would cost more than it saves)
-  constexpr int64_t kAutoWaveSyncTiles = 8;
+  // ---- wave barrier: on request, or automatically when (a) each cluster runs at least kAutoWaveSyncTiles tiles (the
+  // drift the barrier removes builds up over a cluster's tiles) and (b) one wave's operand panels are too big to stay
+  // in L2 between the reads of the tiles that share them: a wave of n cluster tiles (rows x cols, each tile BMp x W,
+  // rows * cols = n) touches K-long panels of at least 2 * K * 2 * sqrt(n * BMp * W) bytes (the square-ish wave;
+  // AM-GM). Measured under Nsight Compute: 256x512 pair tiles gain 1.4 % at 8192^3 (a 102 MB wave), 3.6 % at
+  // 12288^3 and 7 % at 16384^3 and are even at 6144^3 (77 MB); 256x256 pair tiles lose 2 % at 4096^3 (36 MB), where
+  // the waits cost more than the barrier saves.
+  constexpr int64_t kAutoWaveSyncTiles = 4;
+  constexpr double kAutoWaveSyncBytes = 96e6;   // about three quarters of the 126 MB L2
   const bool wave_ok = c.kind == BG_KIND_WS && sk == 1 && n_entries > nclusters;
-  const bool wave = wave_ok && (c.wave_sync == 1 || (c.wave_sync == 0 && n_entries >= kAutoWaveSyncTiles * nclusters));
+  const double wave_bytes =
+      4.0 * static_cast<double>(K) *
+      std::sqrt(static_cast<double>(std::min<int64_t>(nclusters, n_entries)) * bm * cl * static_cast<double>(width));
+  const bool wave_auto = n_entries >= kAutoWaveSyncTiles * nclusters && wave_bytes >= kAutoWaveSyncBytes;
+  const bool wave = wave_ok && (c.wave_sync == 1 || (c.wave_sync == 0 && wave_auto));
   p->wave_per_launch = 0;
   if (wave) {
     for (int64_t j = 1; j * nclusters < n_entries; ++j)

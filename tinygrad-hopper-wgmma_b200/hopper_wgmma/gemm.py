@@ -163,7 +163,8 @@ class WSCfg:
                                # None = for CTA-pair tiles only (see reads_b_directly)
   wave_sync: bool | None = None  # the TMA producers of all CTAs meet at every tile boundary, keeping a wave's tiles
                                # in step so that they share operand panels through L2: True = on, False = off,
-                               # None = on for schedules of at least 8 tiles per cluster (no split-K)
+                               # None = on when each cluster runs >= 4 tiles and a wave's K-long operand panels
+                               # outgrow L2 (256x512 pair tiles from K = 8192; no split-K)
 
   def __post_init__(self):
     if self.BK != 64: raise ValueError("BK must be 64 (one 128-byte swizzle atom)")
