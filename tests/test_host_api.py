@@ -40,14 +40,14 @@ def test_library_reports_missing_device_as_runtime_error_not_crash():
 
 
 def test_cfg_struct_layout_matches_header():
-  """The ctypes mirror of bg_cfg has the header's fields in order (12 int32, int64, 7 int32, padded to 8 bytes)."""
+  """The ctypes mirror of bg_cfg has the header's fields in order (12 int32, int64, 8 int32)."""
   import ctypes
   from hopper_wgmma import _capi
   text = (ROOT / "include" / "sm100_gemm.h").read_text()
   body = text[text.index("typedef struct bg_cfg {"):text.index("} bg_cfg;")]
   fields = re.findall(r"int(?:32|64)_t\s+(\w+);", body)
   assert [f for f, _ in _capi.BgCfg._fields_] == fields
-  assert ctypes.sizeof(_capi.BgCfg) == 12 * 4 + 8 + 7 * 4 + 4
+  assert ctypes.sizeof(_capi.BgCfg) == 12 * 4 + 8 + 8 * 4
 
 
 # ----------------------------------------------------------------------------------------------------------------
@@ -106,8 +106,8 @@ def test_b200_knobs_validate():
 
 def test_which_configs_read_b_directly():
   """build_gemm_ws hands B[K,N] to the kernel uncopied when every CTA's share of a tile's columns, and of a
-  half-width tail tile's, is whole 64-column boxes; by default only CTA pairs do (single-CTA tiles measured slower
-  with N-major B). Otherwise it makes the reference's K-major copy."""
+  half-width tail tile's, is whole 64-column boxes; by default CTA pairs and 128 x 256 single-CTA tiles do (smaller
+  single-CTA tiles measured slower with N-major B). Otherwise it makes the reference's K-major copy."""
   import dataclasses
   from hopper_wgmma import WSCfg
   from hopper_wgmma.ladder import B200, LADDER
@@ -115,8 +115,11 @@ def test_which_configs_read_b_directly():
     assert LADDER[name].reads_b_directly, name                 # 256x256 pair tiles, 128 columns per CTA
   assert B200["pair_wide_hilbert"].reads_b_directly             # two N blocks of 128 columns per CTA
   for name in ("role_split", "tma_store", "hilbert"):
-    assert not LADDER[name].reads_b_directly, name             # single-CTA tiles copy by default ...
-    assert dataclasses.replace(LADDER[name], b_nmajor=True).reads_b_directly, name   # ... and can read directly
+    assert LADDER[name].reads_b_directly, name                 # 128 x 256 single-CTA tiles read B directly ...
+    assert not dataclasses.replace(LADDER[name], b_nmajor=False).reads_b_directly, name   # ... unless told not to
+  for name in ("cta_n128", "cta_n64", "m64_n128"):
+    assert not B200[name].reads_b_directly, name               # smaller single-CTA tiles copy by default
+  assert not WSCfg(consumers=1).reads_b_directly                # 64 x 256: M = 64 MMAs, copied too
   forced = {k: dataclasses.replace(v, b_nmajor=True) for k, v in B200.items()}
   assert forced["cta_n128"].reads_b_directly and forced["m64_n128"].reads_b_directly
   assert not forced["cta_n64"].reads_b_directly                # its half-width tail tiles are 32 columns

@@ -216,9 +216,13 @@ class WSCfg:
   def reads_b_directly(self):
     """True when build_gemm_ws hands B[K,N] to the kernel without a transposed copy. N-major B arrives in 64-column
     boxes, so each CTA's share of a tile's columns (and of a half-width tail tile's) must be whole boxes. By default
-    (b_nmajor=None) only CTA pairs read B directly: on a B200 their kernel time is the same with either layout, while
-    single-CTA tiles ran 2-10 % slower with N-major B (Nsight Compute, 1024^3-8192^3)."""
-    if self.b_nmajor is False or (self.b_nmajor is None and not self.paired): return False
+    (b_nmajor=None) B is read directly where the MMA asks shared memory for at most 96 bytes per cycle: CTA pairs
+    (64 B/cycle; the same kernel time with either layout) and 128 x 256 single-CTA tiles (96 B/cycle; within
+    -1.4 % / +2.8 % at 4096^3 / 2048^3). Smaller single-CTA tiles come close to the SM's 128 bytes per cycle of shared
+    memory, where the MN-major operand reads cost 5-15 % (128 x 128: -8 %, 64 x 128: -15 % at 4096^3; Nsight
+    Compute), so they keep the reference's K-major copy."""
+    wide_cta = not self.paired and self.BM == 128 and self.BN >= 256
+    if self.b_nmajor is False or (self.b_nmajor is None and not (self.paired or wide_cta)): return False
     share = self.BN // 2 if self.paired else self.BN
     return share % 64 == 0 and (self.n_mma == 2 or not self.split_tail or (share // 2) % 64 == 0)
   @property
