@@ -557,3 +557,21 @@ def test_wave_sync_timeout_reports_error_and_recovers(cuda_dev):
     good()
     good.check()
     assert gemm_ref.rel_err(to_bits(C), gemm_ref.gemm_f32(a_bits, b_bits)) <= TOL
+
+
+def test_registered_shared_memory_budget_limits_the_ring(cuda_dev):
+  """A caller lowers the dynamic shared memory registered for a kernel name (the reference's
+  runtime.set_dynamic_smem_bytes) before run(): the plan's ring has the stages that fit, and the GEMM is still right."""
+  from hopper_wgmma import WSCfg, build_gemm_ws, runtime
+  cfg = WSCfg(tma_store=True, cluster=2, hilbert=True)
+  M = N = K = 1024
+  holder = {}
+
+  def build():
+    run = build_gemm_ws(N, cfg, M, K, wait_budget_ns=BUDGET_NS)
+    runtime.set_dynamic_smem_bytes(run.kernel_name, 150_000)
+    holder["run"] = run
+    return run
+  worst, launch = run_case(build, M, N, K, cuda_dev, reps=1)
+  assert launch.info()["stages"] == cfg.within_smem(150_000).stages == 3
+  assert worst <= TOL

@@ -209,6 +209,21 @@ def test_make_tensor_map_argument_checks_match_reference(golden):
     assert str(exc.value) == case["error"]
 
 
+def test_builders_register_their_shared_memory_and_run_honours_a_lower_budget():
+  """build_gemm_ws / build_gated_gemm register their dynamic shared memory per kernel name, as the reference's
+  builders do (gemm.py:316, gated.py:65); a lower registered size cuts the plan's ring to the stages that fit."""
+  from hopper_wgmma import GatedCfg, WSCfg, build_gated_gemm, build_gemm_ws, runtime
+  cfg = WSCfg(tma_store=True, cluster=2, hilbert=True)
+  run = build_gemm_ws(4096, cfg)
+  assert runtime.dynamic_smem_bytes(run.kernel_name) == cfg.smem_bytes
+  gated = build_gated_gemm(512, GatedCfg())
+  assert runtime.dynamic_smem_bytes(gated.kernel_name) == GatedCfg().smem_bytes
+  small = cfg.within_smem(150_000)
+  assert small.stages == 3 and small.smem_bytes <= 150_000 and cfg.within_smem(cfg.smem_bytes) is cfg
+  with pytest.raises(ValueError, match="fewer than 2 stages"):
+    cfg.within_smem(60_000)
+
+
 def test_runtime_hooks_are_compatible_noops():
   from hopper_wgmma.runtime import install_runtime_hooks, set_dynamic_smem_bytes
   install_runtime_hooks()

@@ -10,7 +10,7 @@ from __future__ import annotations
 
 from dataclasses import dataclass
 
-from . import _capi
+from . import _capi, runtime
 from .gemm import SMEM_ALIGN_SLACK, SMEM_LIMIT, Ring, _make_launch
 from .tensors import current_stream, operand, transpose_contiguous
 
@@ -62,6 +62,7 @@ def build_gated_gemm(N: int, cfg: GatedCfg, *, wait_budget_ns: int = 0, debug_sk
   NK = N // BK
   if NK < QS: raise ValueError(f"K has {NK} blocks, fewer than {QS} stages")
   kernel_name = f"sm100_gated_{N}_c{cfg.consumers}_s{QS}_n{BN}"
+  runtime.set_dynamic_smem_bytes(kernel_name, cfg.smem_bytes)   # as the reference's builder does (gated.py:65)
 
   def run(A, B, Cout):
     a, b, c = operand(A), operand(B), operand(Cout)

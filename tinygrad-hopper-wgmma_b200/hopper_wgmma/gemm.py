@@ -22,7 +22,7 @@ from __future__ import annotations
 
 from dataclasses import dataclass
 
-from . import _capi
+from . import _capi, runtime
 from .tensors import current_stream, operand, transpose_contiguous
 
 SMEM_LIMIT = 227 * 1024   # opt-in dynamic shared memory per block on B200 (the same figure as H100/H200)
@@ -212,6 +212,15 @@ class WSCfg:
     return min(8, (SMEM_LIMIT - self.fixed_bytes) // self.stage_bytes)
   @property
   def smem_bytes(self): return self.fixed_bytes + self.stage_bytes * self.stages_used
+  def within_smem(self, nbytes: int) -> "WSCfg":
+    """This config with its shared-memory ring cut to the stages that fit in ``nbytes`` of dynamic shared memory
+    (unchanged when they all fit). ValueError if not even two stages fit."""
+    import dataclasses
+    if self.smem_bytes <= nbytes: return self
+    stages = min(self.stages_used, (nbytes - self.fixed_bytes) // self.stage_bytes)
+    if stages < 2: raise ValueError(f"{nbytes} bytes of dynamic shared memory hold fewer than 2 stages of {self.name}")
+    return dataclasses.replace(self, stages=stages)
+
   @property
   def reads_b_directly(self):
     """True when build_gemm_ws hands B[K,N] to the kernel without a transposed copy. N-major B arrives in 64-column
@@ -319,21 +328,25 @@ def build_gemm_ws(N: int, cfg: WSCfg, M: int | None = None, K: int | None = None
   _, grouped_2d = grouped_tile_order(CMT, NT, min(max(cfg.group_m // CL, 1), CMT), min(cfg.group_n, NT))
   shp = f"{N}" if M == N == K else f"{M}x{N}x{K}"
   kernel_name = f"sm100_{shp}_{'' if grouped_2d else 'g1d_'}{cfg.name}"
+  runtime.set_dynamic_smem_bytes(kernel_name, cfg.smem_bytes)   # as the reference's builder does (gemm.py:316)
 
   def run(A, B, Cout):
+    # the registered size is this kernel's shared-memory budget (a caller may have lowered it since the build)
+    budget = runtime.dynamic_smem_bytes(kernel_name)
+    plan_cfg = cfg if budget is None else cfg.within_smem(budget)
     a, b, c = operand(A), operand(B), operand(Cout)
     if a.shape != (M, K) or b.shape != (K, N) or c.shape != (M, N): raise ValueError("A, B and C shapes do not match the GEMM")
     if not (a.bf16 and b.bf16 and c.bf16): raise ValueError("A, B and C must be bfloat16")
     if not (a.device == b.device == c.device): raise ValueError("A, B and C must be on the same device")
-    if cfg.reads_b_directly:
+    if plan_cfg.reads_b_directly:
       # B as given, N-major: no transposed copy (the reference makes one per run, gemm.py:382)
-      plan = _capi.Plan(cfg.to_c(_capi.KIND_WS, wait_budget_ns=wait_budget_ns, debug_skip_job=debug_skip_job,
+      plan = _capi.Plan(plan_cfg.to_c(_capi.KIND_WS, wait_budget_ns=wait_budget_ns, debug_skip_job=debug_skip_job,
                                  b_nmajor=True), M, N, K, a.ptr, a.row_pitch, b.ptr, b.row_pitch, c.ptr, c.row_pitch,
                         a.device)
       return _make_launch(plan, lambda: current_stream(Cout), Cout, (A, B, Cout))
     BT = transpose_contiguous(B)          # K-major B. Keep it alive: the tensor map holds its raw device pointer
     bt = operand(BT)
-    plan = _capi.Plan(cfg.to_c(_capi.KIND_WS, wait_budget_ns=wait_budget_ns, debug_skip_job=debug_skip_job), M, N, K,
+    plan = _capi.Plan(plan_cfg.to_c(_capi.KIND_WS, wait_budget_ns=wait_budget_ns, debug_skip_job=debug_skip_job), M, N, K,
                       a.ptr, a.row_pitch, bt.ptr, bt.row_pitch, c.ptr, c.row_pitch, a.device)
     return _make_launch(plan, lambda: current_stream(Cout), Cout, (A, BT, Cout))
   run.out_dtype = "bfloat16"
