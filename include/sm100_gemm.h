@@ -37,8 +37,7 @@ enum {
   BG_ERR_EPILOGUE = 4,   /* epilogue timed out waiting for a finished accumulator */
   BG_ERR_DRAIN = 5,      /* final wait for outstanding MMAs timed out             */
   BG_ERR_LOAD_DRAIN = 6, /* wait for in-flight loads after another error timed out */
-  BG_ERR_SPLIT_K = 7,    /* split-K (one wave): a tile's other splits did not all publish in time */
-  BG_ERR_WAVE_SYNC = 8   /* wave barrier: the other CTAs did not all reach a tile boundary in time */
+  BG_ERR_SPLIT_K = 7     /* split-K (one wave): a tile's other splits did not all publish in time */
 };
 
 /*
@@ -86,9 +85,12 @@ enum {
  *               least 4 tiles and whose waves touch operand panels too big to stay in L2 (at least 96 MB by the
  *               estimate 4 K sqrt(clusters x tile rows x tile columns) bytes: 256x512 pair tiles from K = 8192),
  *               off otherwise; 1: on (persistent kernel, no split-K); 2: off. When on, the TMA
- *               producers of all CTAs meet at every tile boundary (a bounded wait on a plan-owned 64-bit counter),
- *               so the tiles of one wave stay in step and share their operand panels through L2; without it CTAs
- *               drift apart over many tiles and re-read the panels from DRAM. Not used by bg_gemm_noalloc.
+ *               producers of all CTAs meet at every tile boundary (a wait on a plan-owned 64-bit counter), so the
+ *               tiles of one wave stay in step and share their operand panels through L2; without it CTAs drift
+ *               apart over many tiles and re-read the panels from DRAM. The barrier orders no data and is soft: a
+ *               CTA that has waited 200 us at one boundary (its launch is not wholly resident, e.g. beside another
+ *               launch on the same GPU) stops waiting for the rest of that launch; results never depend on it.
+ *               Not used by bg_gemm_noalloc.
  */
 typedef struct bg_cfg {
   int32_t kind;

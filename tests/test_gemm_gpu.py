@@ -575,3 +575,31 @@ def test_registered_shared_memory_budget_limits_the_ring(cuda_dev):
   worst, launch = run_case(build, M, N, K, cuda_dev, reps=1)
   assert launch.info()["stages"] == cfg.within_smem(150_000).stages == 3
   assert worst <= TOL
+
+
+def test_wave_sync_launches_side_by_side_on_two_streams(cuda_dev):
+  """Two wave-barrier launches of full-GPU persistent grids on two streams at once: their CTAs cannot all be
+  resident together, and the soft barrier must let both finish correctly without reporting an error."""
+  torch = _torch()
+  from hopper_wgmma import WSCfg, build_gemm_ws
+  from oracle import gemm_ref
+  M, N, K = 2048, 4096, 512
+  cfg = WSCfg(tma_store=True, cluster=2, hilbert=True, wave_sync=True)   # 128 tiles on 74 clusters
+  runs = []
+  for seed in (30, 31):
+    a_bits, b_bits = inputs(M, N, K, seed=seed)
+    A, B = to_dev(a_bits, cuda_dev), to_dev(b_bits, cuda_dev)
+    C = torch.empty((M, N), dtype=torch.bfloat16, device=cuda_dev)
+    poison(C)
+    runs.append((a_bits, b_bits, C, build_gemm_ws(N, cfg, M, K, wait_budget_ns=BUDGET_NS)(A, B, C)))
+  assert "wavesync" in runs[0][3].info()["kernel"]
+  streams = [torch.cuda.Stream(device=cuda_dev) for _ in runs]
+  torch.cuda.synchronize(cuda_dev)
+  for _ in range(5):
+    for st, (_, _, _, launch) in zip(streams, runs):
+      with torch.cuda.stream(st):
+        launch()
+  for st, (a_bits, b_bits, C, launch) in zip(streams, runs):
+    with torch.cuda.stream(st):
+      launch.check()
+    assert gemm_ref.rel_err(to_bits(C), gemm_ref.gemm_f32(a_bits, b_bits)) <= TOL

@@ -762,6 +762,7 @@ int32_t setup_plan(const bg_cfg& c, int64_t M, int64_t N, int64_t K, const void*
   kp.wave_sync = wave ? 1 : 0;
   kp.wave_ctr = nullptr;
   kp.wave_base = 0;
+  kp.wave_wait_ns = 200000;   // 200 us: a boundary's natural spread is a few us (a few % of one tile)
   // A cooperative launch guarantees that every CTA is resident at once. It cannot be combined with cluster
   // dimensions here (such a launch fails under Nsight Compute), so CTA pairs rely on the persistent grid being
   // capped at what the GPU co-schedules, with the bounded wait reporting an error if other work holds SMs.
@@ -972,10 +973,9 @@ int32_t bg_plan_check_error(bg_plan* p, void* stream, uint32_t* err_word) {
     }
     static const char* roles[] = {"?", "producer (free stage)", "MMA (loaded stage)", "MMA (free accumulator)",
                                   "epilogue (finished accumulator)", "MMA drain", "load drain",
-                                  "split-K (partial sums of the tile's other splits)",
-                                  "wave barrier (other CTAs at a tile boundary)"};
+                                  "split-K (partial sums of the tile's other splits)"};
     const uint32_t role = w >> 24;
-    return fail(6, "device wait timed out: %s, counter %u (error word 0x%08x)", role < 9 ? roles[role] : "?",
+    return fail(6, "device wait timed out: %s, counter %u (error word 0x%08x)", role < 8 ? roles[role] : "?",
                 w & 0xFFFFFFu, w);
   }
   return 0;

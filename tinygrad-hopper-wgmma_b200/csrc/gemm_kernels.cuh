@@ -54,7 +54,6 @@ enum : uint32_t {
   kErrDrain = 5u << 24,       // final wait for outstanding MMAs timed out
   kErrLoadDrain = 6u << 24,   // producer's final wait for its in-flight loads timed out (after another error)
   kErrSplitK = 7u << 24,      // split-K (one wave): the other entries of a tile did not all publish in time
-  kErrWaveSync = 8u << 24,    // wave barrier: the other CTAs did not all reach the tile boundary in time
 };
 
 struct GemmParams {
@@ -99,6 +98,7 @@ struct GemmParams {
   int wave_sync;           // 1: the producers of all CTAs meet at every tile boundary (see wave_barrier)
   unsigned long long* wave_ctr;   // wave barrier: arrivals, counted across launches (the plan's counter)
   unsigned long long wave_base;   // wave barrier: the counter's value when this launch starts
+  unsigned long long wave_wait_ns;  // wave barrier: longest wait at one boundary before the CTA stops waiting
   int32_t first_wave[kFirstWave];  // sched[0 .. min(tiles, kFirstWave)) again, delivered with the launch
 };
 
@@ -125,10 +125,12 @@ __device__ __forceinline__ void record_error(unsigned int* err, uint32_t role, u
 // over many tiles (a few percent of speed accumulates to whole tiles), so the tiles of one wave that share an A or B
 // panel no longer read its K-slabs at about the same time, and L2 no longer serves the later readers: at 32768^3 on
 // one GPU (110 tiles per cluster) DRAM read 51x the compulsory bytes. The barrier keeps a wave's tiles within the
-// last tile's spread of each other. It publishes no data (relaxed counting); the wait is bounded. The counter counts
-// across launches: launch L starts at p.wave_base = L x (arrivals per launch), set by the host.
-__device__ __forceinline__ bool wave_barrier(const GemmParams& p, int i, uint64_t budget, int lane) {
-  bool ok = true;
+// last tile's spread of each other. It publishes no data (relaxed counting), so it is soft: a CTA that has waited
+// p.wave_wait_ns at one boundary (the launch's CTAs are not all resident, e.g. beside another launch on the GPU)
+// stops waiting for the rest of the launch (`waiting` turns false) but keeps counting its arrivals, so that the next
+// launch's base stays right. The counter counts across launches: launch L starts at p.wave_base = L x (arrivals per
+// launch), set by the host.
+__device__ __forceinline__ void wave_barrier(const GemmParams& p, int i, int lane, bool& waiting) {
   if (lane == 0) {
     // arrivals at boundaries 1..i: every CTA of each cluster that has a j-th tile
     unsigned long long target = p.wave_base;
@@ -137,19 +139,18 @@ __device__ __forceinline__ bool wave_barrier(const GemmParams& p, int i, uint64_
       target += static_cast<unsigned long long>(left < p.nclusters ? left : p.nclusters) * p.cl;
     }
     atomicAdd(p.wave_ctr, 1ull);
-    if (ld_relaxed_gpu_u64(p.wave_ctr) < target) {
+    if (waiting && ld_relaxed_gpu_u64(p.wave_ctr) < target) {
       const uint64_t t0 = globaltimer_ns();
       while (ld_relaxed_gpu_u64(p.wave_ctr) < target) {
-        if (globaltimer_ns() - t0 > budget) {
-          ok = false;
+        if (globaltimer_ns() - t0 > p.wave_wait_ns) {
+          waiting = false;
           break;
         }
         __nanosleep(64);
       }
     }
   }
-  ok = __shfl_sync(0xffffffffu, ok ? 1u : 0u, 0) != 0;
-  return ok;
+  waiting = __shfl_sync(0xffffffffu, waiting ? 1u : 0u, 0) != 0;
 }
 
 constexpr int kNarrowTile = 0x8000;   // column-field flag of a half-width tile (the last wave's split tiles)
@@ -305,13 +306,11 @@ __global__ void __launch_bounds__(kWsThreads, 1)
     uint32_t stage = 0, phase = 0;
     int job = 0;
     bool failed = false;
+    bool wave_waiting = true;   // the wave barrier still waits (see wave_barrier)
     for (int i = 0; !failed; ++i) {
       const int idx = cid + i * p.nclusters;
       if (idx >= p.tiles) break;
-      if (p.wave_sync && i > 0 && !wave_barrier(p, i, budget, lane)) {
-        if (lane == 0) record_error(p.err, kErrWaveSync, i);
-        break;
-      }
+      if (p.wave_sync && i > 0) wave_barrier(p, i, lane, wave_waiting);
       int cm, tn;
       bool narrow;
       first.coords(p, idx, cm, tn, narrow);
