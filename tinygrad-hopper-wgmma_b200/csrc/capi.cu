@@ -214,7 +214,7 @@ struct bg_plan {
   unsigned int* d_tickets = nullptr;
   WsKernel ws = nullptr;
   RingKernel ring = nullptr;
-  char name[96] = "";
+  char name[128] = "";   // bg_plan_info.kernel receives its first 95 characters
 };
 
 namespace {
@@ -998,7 +998,7 @@ int32_t bg_plan_get_info(const bg_plan* p, bg_plan_info* info) {
   info->max_active_clusters = p->max_active_clusters;
   info->narrow_tiles = p->narrow_tiles;
   info->split_k = p->kp.split_k;
-  snprintf(info->kernel, sizeof(info->kernel), "%s", p->name);
+  snprintf(info->kernel, sizeof(info->kernel), "%.95s", p->name);
   return 0;
 }
 
