@@ -105,3 +105,18 @@ def test_noalloc_entry_checks_arguments_first():
   cfg = _cfg(split_k=2)
   st = lib.bg_gemm_noalloc(ctypes.byref(cfg), 512, 512, 512, FAKE_A, 512, FAKE_B, 512, FAKE_C, 512, 0, None, None)
   assert st < 0 and "split-K" in _capi.last_error()
+
+
+def test_plan_destructor_needs_no_module_globals(monkeypatch):
+  """Plan.__del__ may run at interpreter exit, after the _capi module's globals (ctypes, LIB) have been set to None:
+  it must destroy the handle with what the instance holds."""
+  import ctypes
+  from hopper_wgmma import _capi
+  destroyed = []
+  p = _capi.Plan.__new__(_capi.Plan)
+  p._h = ctypes.c_void_p(1)
+  p._destroy = destroyed.append
+  monkeypatch.setattr(_capi, "ctypes", None)
+  monkeypatch.setattr(_capi, "LIB", None)
+  p.__del__()
+  assert len(destroyed) == 1 and p._h is None

@@ -132,7 +132,8 @@ class Plan:
     return out
 
   def __del__(self):
+    # may run at interpreter exit, after module globals (ctypes included) are gone: use only what the instance holds
     h = getattr(self, "_h", None)
     if h is not None and h.value:
       self._destroy(h)
-      self._h = ctypes.c_void_p()
+      self._h = None
