@@ -94,6 +94,17 @@ enum {
  *               CTA that has waited 200 us at one boundary (its launch is not wholly resident, e.g. beside another
  *               launch on the same GPU) stops waiting for the rest of that launch; results never depend on it.
  *               Not used by bg_gemm_noalloc.
+ *   split_k_cluster  how a split-K plan (split_k > 1, or chosen by -1) reduces its splits. 0 (default):
+ *               automatic — inside a cluster when the plan allows it (below), through the workspace otherwise;
+ *               1: inside a cluster, or fail; 2: through the workspace. Inside a cluster, the split_k splits of a
+ *               tile run on the CTAs of one cluster of split_k CTAs (its ranks), and the tile's columns are shared
+ *               out among them: each CTA sends the columns it does not own straight from tensor memory into their
+ *               owner's shared memory (distributed shared memory, st.async), adds what it receives for its own
+ *               columns in split order and stores them. No workspace and no global-memory round trip; the same
+ *               bits as the workspace. Needs single-CTA tiles (cluster 1, n_mma 1), split_k 2 or 4, each CTA's
+ *               share of the tile's columns a multiple of 64 (32 with the register epilogue), room for the
+ *               received sums ((split_k - 1) * 128 * width / split_k * 4 bytes of shared memory) and every tile
+ *               on its own cluster at once (one wave).
  */
 typedef struct bg_cfg {
   int32_t kind;
@@ -117,6 +128,7 @@ typedef struct bg_cfg {
   int32_t no_k_serpentine;
   int32_t b_nmajor;
   int32_t wave_sync;
+  int32_t split_k_cluster;
 } bg_cfg;
 
 /* What a plan resolved to (for reports and tests). */

@@ -53,6 +53,9 @@ def _cfg(**kw):
   ({"b_nmajor": 1, "kind": 1}, (512, 512, 512), "b_nmajor needs the warp-specialized kernel"),
   ({"b_nmajor": 1, "BN": 96}, (512, 576, 512), "b_nmajor needs BN a multiple of 64"),
   ({"b_nmajor": 1, "BN": 64, "cluster": 2}, (512, 512, 512), "b_nmajor needs BN / 2 a multiple of 64"),
+  ({"wave_sync": 3}, (512, 512, 512), "wave_sync must be 0 (auto), 1 (on) or 2 (off)"),
+  ({"split_k_cluster": 3}, (512, 512, 512), "split_k_cluster must be 0 (auto)"),
+  ({"split_k_cluster": -1}, (512, 512, 512), "split_k_cluster must be 0 (auto)"),
 ])
 def test_contract_violations_are_negative_status(kw, shape, msg):
   st, err = _create(_cfg(**kw), *shape)

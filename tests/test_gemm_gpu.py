@@ -368,7 +368,7 @@ def test_ragged_shapes(idx, cuda_dev):
 def _split_k_cases():
   from hopper_wgmma import WSCfg
   return [
-    ("cta_tmast_sk2", WSCfg(BN=128, tma_store=True, hilbert=True, split_k=2), (512, 512, 1024)),
+    ("cta_tmast_sk2", WSCfg(BN=128, tma_store=True, hilbert=True, split_k=2, split_k_cluster=False), (512, 512, 1024)),
     ("cta_reg_sk3_uneven_k", WSCfg(BN=128, split_k=3), (256, 256, 448)),               # 7 k-blocks: 2 + 2 + 3
     ("bm64_sk4", WSCfg(consumers=1, BN=128, tma_store=True, split_k=4), (256, 512, 512)),
     ("pair_tmast_sk2", WSCfg(tma_store=True, cluster=2, hilbert=True, split_k=2), (512, 512, 512)),
@@ -379,7 +379,7 @@ def _split_k_cases():
     ("one_kblock_each_sk8", WSCfg(BN=64, tma_store=True, split_k=8), (128, 256, 512)),
     ("ragged_pair_sk2", WSCfg(tma_store=True, cluster=2, ragged=True, split_k=2), (300, 520, 1000)),
     ("pair_sk5_few_clusters", WSCfg(cluster=2, split_k=5, num_sm=8), (512, 256, 640)),
-    ("small_ring_sk2", WSCfg(BN=128, stages=3, split_k=2), (256, 512, 1024)),        # reduce through registers
+    ("small_ring_sk2", WSCfg(BN=128, stages=3, split_k=2, split_k_cluster=False), (256, 512, 1024)),   # registers
     ("bm64_reg_sk6", WSCfg(consumers=1, BN=64, split_k=6), (192, 256, 768)),
   ]
 
@@ -392,7 +392,7 @@ def test_split_k(idx, cuda_dev):
   name, cfg, (M, N, K) = _split_k_cases()[idx]
   worst, launch = run_case(lambda: build_gemm_ws(N, cfg, M, K, wait_budget_ns=BUDGET_NS), M, N, K, cuda_dev)
   info = launch.info()
-  assert info["split_k"] == cfg.split_k and f"splitk={cfg.split_k}" in info["kernel"]
+  assert info["split_k"] == cfg.split_k and f"splitk={cfg.split_k} " in info["kernel"]   # through the workspace
   assert worst <= TOL, f"{name} {M}x{N}x{K}: relative_error={worst:.5f} ({info['kernel']})"
 
 
@@ -420,7 +420,7 @@ def test_split_k_timeout_reports_error_and_plans_recover(cuda_dev):
   the stuck one times out, the launch reports the error and the host clears the arrival words."""
   torch = _torch()
   from hopper_wgmma import WSCfg, build_gemm_ws
-  cfg = WSCfg(BN=128, tma_store=True, split_k=2)
+  cfg = WSCfg(BN=128, tma_store=True, split_k=2, split_k_cluster=False)
   M = N = K = 256
   A = torch.zeros((M, K), dtype=torch.bfloat16, device=cuda_dev)
   B = torch.zeros((K, N), dtype=torch.bfloat16, device=cuda_dev)
@@ -447,6 +447,107 @@ def test_split_k_auto_choice(cuda_dev):
   _, launch = run_case(lambda: build_gemm_ws(1024, cfg, 1024, 1024, wait_budget_ns=BUDGET_NS), 1024, 1024, 1024,
                        cuda_dev, reps=1)
   assert launch.info()["split_k"] == 1            # 16 k-blocks: too short to split
+
+
+# ------------------------------------------------------------------------------------------------------------------
+# split-K inside a cluster (split_k_cluster): the splits of a tile are the CTAs of one cluster and add up through
+# distributed shared memory
+# ------------------------------------------------------------------------------------------------------------------
+def _split_k_cluster_cases():
+  from hopper_wgmma import WSCfg
+  return [
+    ("cta_tmast_sk2", WSCfg(BN=128, tma_store=True, hilbert=True, split_k=2, split_k_cluster=True), (512, 512, 1024)),
+    ("cta_reg_sk2_uneven_k", WSCfg(BN=128, split_k=2, split_k_cluster=True), (256, 384, 448)),   # 7 k-blocks: 3 + 4
+    ("cta_bn256_sk2_b_as_given", WSCfg(BN=256, tma_store=True, split_k=2, split_k_cluster=True), (256, 512, 1024)),
+    ("cta_bn256_sk4", WSCfg(BN=256, tma_store=True, split_k=4, split_k_cluster=True), (256, 512, 2048)),
+    ("cta_reg_sk4_32_columns_each", WSCfg(BN=128, split_k=4, split_k_cluster=True), (256, 256, 1024)),
+    ("bm64_sk2", WSCfg(consumers=1, BN=128, tma_store=True, split_k=2, split_k_cluster=True), (192, 256, 512)),
+    ("bn64_reg_sk2", WSCfg(BN=64, split_k=2, split_k_cluster=True), (256, 192, 640)),
+    ("ragged_sk2", WSCfg(BN=128, tma_store=True, ragged=True, split_k=2, split_k_cluster=True), (300, 520, 1000)),
+    ("one_kblock_each_sk4", WSCfg(BN=256, tma_store=True, split_k=4, split_k_cluster=True), (128, 256, 256)),
+    ("auto_picks_cluster", WSCfg(BN=128, tma_store=True, split_k=2), (384, 512, 2048)),
+  ]
+
+
+@pytest.mark.parametrize("idx", range(10))
+def test_split_k_in_cluster(idx, cuda_dev):
+  """Three launches of one plan on NaN-poisoned C, against the CPU oracle: every tile's splits run on one cluster and
+  exchange their sums through distributed shared memory (the plan's kernel name says so)."""
+  from hopper_wgmma import build_gemm_ws
+  name, cfg, (M, N, K) = _split_k_cluster_cases()[idx]
+  worst, launch = run_case(lambda: build_gemm_ws(N, cfg, M, K, wait_budget_ns=BUDGET_NS), M, N, K, cuda_dev)
+  info = launch.info()
+  assert info["split_k"] == cfg.split_k and f"splitk={cfg.split_k}/cluster" in info["kernel"], info["kernel"]
+  assert info["grid"] == cfg.split_k * info["tiles"]
+  assert worst <= TOL, f"{name} {M}x{N}x{K}: relative_error={worst:.5f} ({info['kernel']})"
+
+
+@pytest.mark.parametrize("cfg_name", ["sk2_tma_store", "sk4_registers"])
+def test_split_k_cluster_matches_the_workspace_bitwise(cfg_name, cuda_dev):
+  """Both protocols add the splits in split order 0, 1, ..., S - 1 onto the same per-split sums, so their outputs
+  agree bit for bit."""
+  import dataclasses
+  torch = _torch()
+  from hopper_wgmma import WSCfg, build_gemm_ws
+  base, (M, N, K) = {
+    "sk2_tma_store": (WSCfg(BN=128, tma_store=True, hilbert=True, split_k=2), (512, 768, 1536)),
+    "sk4_registers": (WSCfg(BN=128, split_k=4), (384, 512, 2048)),
+  }[cfg_name]
+  a_bits, b_bits = inputs(M, N, K, seed=23)
+  A, B = to_dev(a_bits, cuda_dev), to_dev(b_bits, cuda_dev)
+  outs = {}
+  for in_cluster in (True, False):
+    C = torch.empty((M, N), dtype=torch.bfloat16, device=cuda_dev)
+    poison(C)
+    cfg = dataclasses.replace(base, split_k_cluster=in_cluster)
+    launch = build_gemm_ws(N, cfg, M, K, wait_budget_ns=BUDGET_NS)(A, B, C)
+    launch()
+    launch.check()
+    assert ("/cluster" in launch.info()["kernel"]) == in_cluster
+    outs[in_cluster] = to_bits(C)
+  assert (outs[True] == outs[False]).all()
+
+
+def test_split_k_cluster_timeout_reports_error_and_plans_recover(cuda_dev):
+  """K = 320 splits 2 + 3 k-blocks: only split 1 has a job 2, which its producer skips, so split 0 sends its share,
+  waits for split 1's in vain and reports the timeout; the context stays usable and the next plan is right."""
+  torch = _torch()
+  from hopper_wgmma import WSCfg, build_gemm_ws
+  cfg = WSCfg(BN=128, tma_store=True, split_k=2, split_k_cluster=True)
+  M, N, K = 256, 256, 320
+  A = torch.zeros((M, K), dtype=torch.bfloat16, device=cuda_dev)
+  B = torch.zeros((K, N), dtype=torch.bfloat16, device=cuda_dev)
+  C = torch.empty((M, N), dtype=torch.bfloat16, device=cuda_dev)
+  bad = build_gemm_ws(N, cfg, M, K, wait_budget_ns=50_000_000, debug_skip_job=2)(A, B, C)
+  bad()
+  with pytest.raises(RuntimeError, match="timed out"):
+    bad.check()
+  worst, _ = run_case(lambda: build_gemm_ws(N, cfg, M, K, wait_budget_ns=BUDGET_NS), M, N, K, cuda_dev, reps=2)
+  assert worst <= TOL
+
+
+@pytest.mark.parametrize("case", ["pair", "three_splits", "narrow_share", "too_many_tiles"])
+def test_split_k_cluster_refusals(case, cuda_dev):
+  """split_k_cluster=True where a cluster cannot hold the splits fails before any launch, naming the reason; the
+  automatic choice falls back to the workspace on the same plan."""
+  import dataclasses
+  torch = _torch()
+  from hopper_wgmma import WSCfg, build_gemm_ws
+  cfg, (M, N, K), why = {
+    "pair": (WSCfg(tma_store=True, cluster=2, split_k=2), (512, 512, 512), "single-CTA tiles"),
+    "three_splits": (WSCfg(BN=128, split_k=3), (256, 256, 768), "split_k 2 or 4"),
+    "narrow_share": (WSCfg(BN=128, tma_store=True, split_k=4), (256, 256, 1024), "multiple of 64"),
+    "too_many_tiles": (WSCfg(BN=128, tma_store=True, split_k=2), (2048, 2048, 512), "own cluster"),
+  }[case]
+  A = torch.zeros((M, K), dtype=torch.bfloat16, device=cuda_dev)
+  B = torch.zeros((K, N), dtype=torch.bfloat16, device=cuda_dev)
+  C = torch.empty((M, N), dtype=torch.bfloat16, device=cuda_dev)
+  with pytest.raises((RuntimeError, ValueError), match=why):
+    build_gemm_ws(N, dataclasses.replace(cfg, split_k_cluster=True), M, K)(A, B, C)
+  launch = build_gemm_ws(N, cfg, M, K, wait_budget_ns=BUDGET_NS)(A, B, C)
+  assert "/cluster" not in launch.info()["kernel"]
+  launch()
+  launch.check()
 
 
 def test_plan_tables_hold_bounded_device_memory(cuda_dev):

@@ -40,14 +40,14 @@ def test_library_reports_missing_device_as_runtime_error_not_crash():
 
 
 def test_cfg_struct_layout_matches_header():
-  """The ctypes mirror of bg_cfg has the header's fields in order (12 int32, int64, 8 int32)."""
+  """The ctypes mirror of bg_cfg has the header's fields in order (12 int32, int64, 9 int32, padded to 8 bytes)."""
   import ctypes
   from hopper_wgmma import _capi
   text = (ROOT / "include" / "sm100_gemm.h").read_text()
   body = text[text.index("typedef struct bg_cfg {"):text.index("} bg_cfg;")]
   fields = re.findall(r"int(?:32|64)_t\s+(\w+);", body)
   assert [f for f, _ in _capi.BgCfg._fields_] == fields
-  assert ctypes.sizeof(_capi.BgCfg) == 12 * 4 + 8 + 8 * 4
+  assert ctypes.sizeof(_capi.BgCfg) == 12 * 4 + 8 + 9 * 4 + 4
 
 
 # ----------------------------------------------------------------------------------------------------------------
@@ -102,6 +102,12 @@ def test_b200_knobs_validate():
     WSCfg(BN=48, split_k=2)
   assert WSCfg(split_k=4).name.endswith("_sk4") and WSCfg(split_k=4).to_c().split_k == 4
   assert WSCfg(split_k=-1).name.endswith("_skA") and WSCfg(split_k=-1).to_c().split_k == -1
+  # split_k_cluster: None = automatic (0), True = inside a cluster (1), False = through the workspace (2)
+  assert WSCfg(split_k=2).to_c().split_k_cluster == 0
+  assert WSCfg(split_k=2, split_k_cluster=True).name.endswith("_sk2_skc")
+  assert WSCfg(split_k=2, split_k_cluster=True).to_c().split_k_cluster == 1
+  assert WSCfg(split_k=2, split_k_cluster=False).name.endswith("_sk2_skw")
+  assert WSCfg(split_k=2, split_k_cluster=False).to_c().split_k_cluster == 2
 
 
 def test_which_configs_read_b_directly():

@@ -24,6 +24,9 @@ def test_lookup_modifiers():
   c = lookup("cluster_hilbert@bT")
   assert c.b_nmajor is False and c.cluster == 2 and LADDER["cluster_hilbert"].b_nmajor is None
   assert lookup("cta_n128@bN").b_nmajor is True
+  c = lookup("cta_n128@sk2@skw")
+  assert c.split_k == 2 and c.split_k_cluster is False and lookup("cta_n128@sk2@skc").split_k_cluster is True
+  assert lookup("cta_n128@sk2").split_k_cluster is None
   with pytest.raises(KeyError):
     lookup("cta_n64@bogus")
   with pytest.raises(KeyError):

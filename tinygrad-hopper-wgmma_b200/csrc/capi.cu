@@ -153,7 +153,7 @@ using WsKernel = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMa
 using RingKernel = void (*)(const CUtensorMap, const CUtensorMap, const GemmParams);
 
 // Split-K is a template switch so that the kernels without it carry none of its code or registers.
-template <int NB, bool SK>
+template <int NB, int SK>
 WsKernel pick_ws_nb(int bm, bool paired, bool tma_store) {
   using namespace sm100;
   if (bm == 128) {
@@ -163,9 +163,17 @@ WsKernel pick_ws_nb(int bm, bool paired, bool tma_store) {
   return tma_store ? sm100_gemm_ws<64, false, true, NB, SK> : sm100_gemm_ws<64, false, false, NB, SK>;
 }
 
-WsKernel pick_ws(int bm, bool paired, bool tma_store, int nblk, bool split_k) {
-  if (split_k) return nblk == 2 ? pick_ws_nb<2, true>(bm, paired, tma_store) : pick_ws_nb<1, true>(bm, paired, tma_store);
-  return nblk == 2 ? pick_ws_nb<2, false>(bm, paired, tma_store) : pick_ws_nb<1, false>(bm, paired, tma_store);
+// split: sm100::kSplitNone, kSplitWorkspace or kSplitCluster (single-CTA tiles with one N block only)
+WsKernel pick_ws(int bm, bool paired, bool tma_store, int nblk, int split) {
+  using namespace sm100;
+  if (split == kSplitCluster) {
+    if (paired || nblk != 1) return nullptr;
+    if (bm == 128) return tma_store ? sm100_gemm_ws<128, false, true, 1, kSplitCluster> : sm100_gemm_ws<128, false, false, 1, kSplitCluster>;
+    return tma_store ? sm100_gemm_ws<64, false, true, 1, kSplitCluster> : sm100_gemm_ws<64, false, false, 1, kSplitCluster>;
+  }
+  if (split == kSplitWorkspace)
+    return nblk == 2 ? pick_ws_nb<2, kSplitWorkspace>(bm, paired, tma_store) : pick_ws_nb<1, kSplitWorkspace>(bm, paired, tma_store);
+  return nblk == 2 ? pick_ws_nb<2, kSplitNone>(bm, paired, tma_store) : pick_ws_nb<1, kSplitNone>(bm, paired, tma_store);
 }
 
 RingKernel pick_ring(int bm) { return bm == 128 ? sm100::sm100_gemm_ring<128> : sm100::sm100_gemm_ring<64>; }
@@ -193,6 +201,7 @@ struct bg_plan {
   bool paired = false;
   bool tma_store = false;
   int cl = 1;
+  int kc = 1;   // split-K inside a cluster: CTAs per cluster that share a tile's K (launched cluster = cl * kc)
   int grid = 0;
   int threads = 0;
   size_t smem = 0;
@@ -484,6 +493,8 @@ int32_t setup_plan(const bg_cfg& c, int64_t M, int64_t N, int64_t K, const void*
   if (c.wave_sync < 0 || c.wave_sync > 2) return fail(-1, "wave_sync must be 0 (auto), 1 (on) or 2 (off)");
   if (c.wave_sync == 1 && (c.kind != BG_KIND_WS || sk > 1))
     return fail(-1, "wave_sync needs the persistent kernel without split-K");
+  if (c.split_k_cluster < 0 || c.split_k_cluster > 2)
+    return fail(-1, "split_k_cluster must be 0 (auto), 1 (inside a cluster) or 2 (through the workspace)");
 
   const int bm = 64 * std::max(c.consumers, 1);
   const int cl = c.cluster;
@@ -537,7 +548,7 @@ int32_t setup_plan(const bg_cfg& c, int64_t M, int64_t N, int64_t K, const void*
   const uint32_t b_block = static_cast<uint32_t>(bn_local) * 128u;
   const uint32_t b_stage = b_block * static_cast<uint32_t>(nblk);
   const uint32_t c_bytes = c.tma_store ? static_cast<uint32_t>(bm) * 256u : 0u;
-  const uint32_t fixed = 1024u + c_bytes + (c.kind == BG_KIND_RING ? 16u : 48u);
+  const uint32_t fixed = 1024u + c_bytes + (c.kind == BG_KIND_RING ? 16u : 56u);
   int stages = c.stages;
   if (stages == 0) {
     const int64_t fit = (static_cast<int64_t>(smem_optin) - fixed) / (a_stage + b_stage + 16);
@@ -597,11 +608,79 @@ int32_t setup_plan(const bg_cfg& c, int64_t M, int64_t N, int64_t K, const void*
     p->ring = pick_ring(bm);
     fn = reinterpret_cast<const void*>(p->ring);
   } else {
-    p->ws = pick_ws(bm, paired, p->tma_store, nblk, sk > 1);
+    p->ws = pick_ws(bm, paired, p->tma_store, nblk, sk > 1 ? sm100::kSplitWorkspace : sm100::kSplitNone);
     fn = reinterpret_cast<const void*>(p->ws);
   }
   cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_optin);
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(MaxDynamicSharedMemorySize)");
+
+  // ---- split-K inside a cluster (bg_cfg.split_k_cluster): the sk CTAs of one cluster share each tile and reduce
+  // through distributed shared memory, each receiving (sk - 1) x 128 x (width / sk) fp32 sums (the 4 epilogue
+  // warps' 32 tensor-memory lanes each, also when BM = 64 leaves half of them unused)
+  int kc = 1;
+  uint32_t recv_bytes = 0;
+  if (sk > 1 && c.split_k_cluster != 2) {
+    char why[160] = "";
+    const int share = width % sk == 0 ? width / sk : 0;
+    const int num_sm = c.num_sm > 0 ? c.num_sm : sm_count;
+    int kc_stages = stages;
+    size_t kc_smem = 0;
+    WsKernel kc_fn = nullptr;
+    if (cl != 1 || nblk != 1) {
+      snprintf(why, sizeof(why), "single-CTA tiles (cluster 1, n_mma 1)");
+    } else if (sk != 2 && sk != 4) {
+      snprintf(why, sizeof(why), "split_k 2 or 4 (got %d)", sk);
+    } else if (share == 0 || share % (c.tma_store ? 64 : 32)) {
+      snprintf(why, sizeof(why), "each split's share of the %d tile columns a multiple of %d", width,
+               c.tma_store ? 64 : 32);
+    } else if (tiles * sk > num_sm) {
+      snprintf(why, sizeof(why), "every tile on its own cluster at once (%lld tiles x %d splits > %d SMs)",
+               (long long)tiles, sk, num_sm);
+    } else {
+      recv_bytes = static_cast<uint32_t>(sk - 1) * 128u * static_cast<uint32_t>(share) * 4u;
+      if (c.stages == 0) {
+        const int64_t fit = (static_cast<int64_t>(smem_optin) - fixed - recv_bytes) / (a_stage + b_stage + 16);
+        kc_stages = static_cast<int>(std::min<int64_t>(fit, 8));
+      }
+      kc_smem = fixed + recv_bytes + static_cast<size_t>(kc_stages) * (a_stage + b_stage + 16u);
+      kc_fn = pick_ws(bm, paired, p->tma_store, nblk, sm100::kSplitCluster);
+      if (kc_stages < 2 || kc_smem > static_cast<size_t>(smem_optin)) {
+        snprintf(why, sizeof(why), "room for %u bytes of received sums beside the ring", recv_bytes);
+      } else {
+        e = cudaFuncSetAttribute(reinterpret_cast<const void*>(kc_fn), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 smem_optin);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(MaxDynamicSharedMemorySize)");
+        cudaLaunchConfig_t lc = {};
+        lc.gridDim = dim3(static_cast<unsigned>(sk * tiles));
+        lc.blockDim = dim3(p->threads);
+        lc.dynamicSmemBytes = kc_smem;
+        cudaLaunchAttribute at[1];
+        at[0].id = cudaLaunchAttributeClusterDimension;
+        at[0].val.clusterDim.x = sk;
+        at[0].val.clusterDim.y = 1;
+        at[0].val.clusterDim.z = 1;
+        lc.attrs = at;
+        lc.numAttrs = 1;
+        int maxc = 0;
+        e = cudaOccupancyMaxActiveClusters(&maxc, reinterpret_cast<const void*>(kc_fn), &lc);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveClusters");
+        if (maxc < tiles)
+          snprintf(why, sizeof(why), "every tile on its own cluster at once (%lld tiles, %d clusters of %d fit)",
+                   (long long)tiles, maxc, sk);
+      }
+    }
+    if (why[0] == '\0') {
+      kc = sk;
+      stages = kc_stages;
+      smem = kc_smem;
+      p->ws = kc_fn;
+      fn = reinterpret_cast<const void*>(kc_fn);
+    } else {
+      recv_bytes = 0;
+      if (c.split_k_cluster == 1) return fail(-1, "split_k_cluster = 1 needs %s", why);
+    }
+  }
+  p->kc = kc;
   // Tensor memory is 512 columns per SM. CTAs that could share an SM must fit in it together, or a CTA would block
   // in tcgen05.alloc behind another (and CTA pairs waiting on each other could deadlock). Pad the shared-memory
   // request until the occupancy limit keeps co-resident CTAs within the SM's tensor memory.
@@ -619,15 +698,17 @@ int32_t setup_plan(const bg_cfg& c, int64_t M, int64_t N, int64_t K, const void*
     }
     p->smem = smem;
   }
-  if (cl > 1) {
+  const int lcl = cl * kc;   // CTAs per launched cluster
+  if (kc > 1) nclusters = (c.num_sm > 0 ? c.num_sm : sm_count) / lcl;
+  if (lcl > 1) {
     // Persistent clusters must all be resident at once: cap their number at what the GPU can co-schedule.
     cudaLaunchConfig_t lc = {};
-    lc.gridDim = dim3(static_cast<unsigned>(cl * nclusters));
+    lc.gridDim = dim3(static_cast<unsigned>(lcl * nclusters));
     lc.blockDim = dim3(p->threads);
     lc.dynamicSmemBytes = smem;
     cudaLaunchAttribute at[1];
     at[0].id = cudaLaunchAttributeClusterDimension;
-    at[0].val.clusterDim.x = cl;
+    at[0].val.clusterDim.x = lcl;
     at[0].val.clusterDim.y = 1;
     at[0].val.clusterDim.z = 1;
     lc.attrs = at;
@@ -635,7 +716,7 @@ int32_t setup_plan(const bg_cfg& c, int64_t M, int64_t N, int64_t K, const void*
     int maxc = 0;
     e = cudaOccupancyMaxActiveClusters(&maxc, fn, &lc);
     if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveClusters");
-    if (maxc <= 0) return fail(5, "no cluster of %d CTAs with %zu bytes of shared memory fits on the device", cl, smem);
+    if (maxc <= 0) return fail(5, "no cluster of %d CTAs with %zu bytes of shared memory fits on the device", lcl, smem);
     p->max_active_clusters = maxc;
     if (c.kind == BG_KIND_WS) nclusters = std::min<int64_t>(nclusters, maxc);
   }
@@ -664,8 +745,9 @@ int32_t setup_plan(const bg_cfg& c, int64_t M, int64_t N, int64_t K, const void*
     }
   }
   if (nt * 2 > 0x7FFF) return fail(-1, "too many column tiles (%lld) for the tile table", (long long)nt);
-  // ---- split-K: every tile becomes sk consecutive entries (split s = entry % sk), dealt to consecutive clusters
-  if (sk > 1) {
+  // ---- split-K through the workspace: every tile becomes sk consecutive entries (split s = entry % sk), dealt to
+  // consecutive clusters. (Inside a cluster, each tile keeps one entry: its cluster's ranks are the splits.)
+  if (sk > 1 && kc == 1) {
     std::vector<int32_t> ext;
     ext.reserve(sched.size() * sk);
     for (int32_t e : sched)
@@ -677,9 +759,9 @@ int32_t setup_plan(const bg_cfg& c, int64_t M, int64_t N, int64_t K, const void*
     p->ticket_words = static_cast<size_t>(tiles) * cl * 4u;
   }
   // one entry per cluster: the tile's entries are all resident together (cooperative launch) and share the reduce
-  const bool sk_scatter = sk > 1 && n_entries <= nclusters;
+  const bool sk_scatter = sk > 1 && kc == 1 && n_entries <= nclusters;
   nclusters = std::min<int64_t>(nclusters, n_entries);
-  p->grid = static_cast<int>(nclusters * (c.kind == BG_KIND_RING ? 1 : cl));
+  p->grid = static_cast<int>(nclusters * (c.kind == BG_KIND_RING ? 1 : lcl));
 
   // ---- tensor maps: A[M,K] box (64, BM); BT[N,K] box (64, bn_local), or B[K,N] box (64, 64) when N-major;
   // C[M,N] box (64, BM/4) per epilogue warp
@@ -763,6 +845,8 @@ int32_t setup_plan(const bg_cfg& c, int64_t M, int64_t N, int64_t K, const void*
   kp.wave_ctr = nullptr;
   kp.wave_base = 0;
   kp.wave_wait_ns = 200000;   // 200 us: a boundary's natural spread is a few us (a few % of one tile)
+  kp.kc = kc;
+  kp.kc_recv_bytes = recv_bytes;
   // A cooperative launch guarantees that every CTA is resident at once. It cannot be combined with cluster
   // dimensions here (such a launch fails under Nsight Compute), so CTA pairs rely on the persistent grid being
   // capped at what the GPU co-schedules, with the bounded wait reporting an error if other work holds SMs.
@@ -773,10 +857,11 @@ int32_t setup_plan(const bg_cfg& c, int64_t M, int64_t N, int64_t K, const void*
   // the first wave of the tile table also travels in the kernel parameters (see FirstTile in the kernel)
   for (size_t i = 0; i < sched.size() && i < static_cast<size_t>(sm100::kFirstWave); ++i) kp.first_wave[i] = sched[i];
 
-  snprintf(p->name, sizeof(p->name), "%s<BM=%d,%s,%s> BN=%dx%d stages=%d acc=%d tail=%d splitk=%d%s b=%s",
+  snprintf(p->name, sizeof(p->name), "%s<BM=%d,%s,%s> BN=%dx%d stages=%d acc=%d tail=%d splitk=%d%s%s b=%s",
            c.kind == BG_KIND_RING ? "sm100_gemm_ring" : "sm100_gemm_ws", bm,
            paired ? "pair" : (cl == 2 ? "cluster2" : "cta"), p->tma_store ? "tma_store" : "reg_store", bn, nblk,
-           stages, acc_bufs, p->narrow_tiles, sk, wave ? " wavesync" : "", nmajor ? "N" : "K");
+           stages, acc_bufs, p->narrow_tiles, sk, kc > 1 ? "/cluster" : "", wave ? " wavesync" : "",
+           nmajor ? "N" : "K");
   return 0;
 }
 
@@ -928,9 +1013,9 @@ int32_t bg_plan_launch(bg_plan* p, void* stream) {
   cudaLaunchAttribute at[2];
   lc.attrs = at;
   lc.numAttrs = 0;
-  if (p->cl > 1 && p->kind == BG_KIND_WS) {
+  if (p->cl * p->kc > 1 && p->kind == BG_KIND_WS) {
     at[lc.numAttrs].id = cudaLaunchAttributeClusterDimension;
-    at[lc.numAttrs].val.clusterDim.x = p->cl;
+    at[lc.numAttrs].val.clusterDim.x = p->cl * p->kc;
     at[lc.numAttrs].val.clusterDim.y = 1;
     at[lc.numAttrs].val.clusterDim.z = 1;
     ++lc.numAttrs;

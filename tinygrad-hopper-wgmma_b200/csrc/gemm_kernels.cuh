@@ -27,8 +27,10 @@
 // even CTA issues MMAs (M = 256 across the pair); the odd CTA's loads complete on the even CTA's barriers and the
 // MMA commits arrive on both CTAs' barriers. No load is multicast.
 // A persistent cluster walks K forwards on its even-numbered tiles and backwards on its odd-numbered ones (K
-// serpentine), and with SPLITK = true the tile table may hold several entries per tile over disjoint K ranges, whose
-// fp32 partial sums the epilogue warps combine through a global workspace (see the split-K block of the epilogue).
+// serpentine). SPLITK selects split-K: with kSplitWorkspace the tile table may hold several entries per tile over
+// disjoint K ranges, whose fp32 partial sums the epilogue warps combine through a global workspace; with
+// kSplitCluster the CTAs of one cluster are the splits of one tile and combine their sums through distributed shared
+// memory (see the split-K block of the epilogue).
 //
 // Every mbarrier wait is bounded (GemmParams::budget_ns). On expiry a thread writes a code into GemmParams::err and
 // leaves its loop; all other roles then run out of work or time out too, the kernel drains what it issued, frees
@@ -43,6 +45,7 @@ constexpr int kWsThreads = 256;   // warps 0-3 producer / MMA / idle, warps 4-7 
 constexpr int kRingThreads = 128;
 constexpr int kFirstWave = 160;   // first-wave tile entries passed in the kernel parameters (>= clusters on a B200)
 constexpr int kSkSlots = 8;
+constexpr int kSplitNone = 0, kSplitWorkspace = 1, kSplitCluster = 2;   // the kernel's SPLITK parameter
 constexpr uint32_t kNmajorChunk = 64 * 128;   // one N-major B box in shared memory: 64 K rows x 64 columns of bf16       // split-K reduce: 4 KB shared-memory slots per epilogue warp (in the idle ring)
 
 // Error word layout: role in bits 24-31, the role's job or tile counter (saturated) in bits 0-23.
@@ -99,15 +102,19 @@ struct GemmParams {
   unsigned long long* wave_ctr;   // wave barrier: arrivals, counted across launches (the plan's counter)
   unsigned long long wave_base;   // wave barrier: the counter's value when this launch starts
   unsigned long long wave_wait_ns;  // wave barrier: longest wait at one boundary before the CTA stops waiting
+  int kc;                  // split-K inside a cluster (1 = off): the kc CTAs of a cluster run splits 0..kc-1 (their
+                           // cluster rank) of the cluster's one tile and reduce through distributed shared memory
+  uint32_t kc_recv_bytes;  // split-K inside a cluster: bytes each CTA receives from the others (its receive region)
   int32_t first_wave[kFirstWave];  // sched[0 .. min(tiles, kFirstWave)) again, delivered with the launch
 };
 
-// K range of schedule entry idx: k-blocks [kb0, kb0 + nk). Kernels built without split-K (SPLITK = false) ignore
-// p.split_k; the host never hands them a split schedule.
-template <bool SPLITK>
-__device__ __forceinline__ void k_range(const GemmParams& p, int idx, int& kb0, int& nk) {
-  if (SPLITK && p.split_k > 1) {
-    const int s = idx % p.split_k;
+// K range of schedule entry idx: k-blocks [kb0, kb0 + nk). Kernels built without split-K (kSplitNone) ignore
+// p.split_k; the host never hands them a split schedule. Split-K inside a cluster runs split `ks` (the CTA's cluster
+// rank) of every entry; through the workspace, entry idx is split idx % split_k of its tile.
+template <int SPLITK>
+__device__ __forceinline__ void k_range(const GemmParams& p, int idx, int ks, int& kb0, int& nk) {
+  if (SPLITK != kSplitNone && p.split_k > 1) {
+    const int s = SPLITK == kSplitCluster ? ks : idx % p.split_k;
     kb0 = s * p.num_kb / p.split_k;
     nk = (s + 1) * p.num_kb / p.split_k - kb0;
   } else {
@@ -238,13 +245,14 @@ __device__ __forceinline__ void epilogue_registers(uint32_t tacc, __nv_bfloat16*
   }
 }
 
-template <int BM, bool PAIRED, bool TMA_STORE, int NB, bool SPLITK>
+template <int BM, bool PAIRED, bool TMA_STORE, int NB, int SPLITK>
 __global__ void __launch_bounds__(kWsThreads, 1)
     sm100_gemm_ws(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                   const __grid_constant__ CUtensorMap tmBn, const __grid_constant__ CUtensorMap tmC,
                   const __grid_constant__ GemmParams p) {
   static_assert(BM == 64 || BM == 128, "BM is 64 or 128 rows per CTA");
   static_assert(!PAIRED || BM == 128, "CTA pairs use M = 256 (128 rows per CTA)");
+  static_assert(SPLITK != kSplitCluster || (!PAIRED && NB == 1), "split-K inside a cluster: single-CTA, one N block");
   constexpr int CG = PAIRED ? 2 : 1;
   constexpr int ROWS_W = BM / 4;                  // accumulator rows per epilogue warp
   constexpr uint32_t STAGE_C = ROWS_W * 128;      // one 64-column bf16 staging buffer of one warp
@@ -255,20 +263,29 @@ __global__ void __launch_bounds__(kWsThreads, 1)
   const uint32_t sA = base;
   const uint32_t sB = sA + p.stages * p.a_stage_bytes;
   const uint32_t sC = sB + p.stages * p.b_stage_bytes;
-  const uint32_t bars = sC + (TMA_STORE ? 4u * 2u * STAGE_C : 0u);
+  const uint32_t sR = sC + (TMA_STORE ? 4u * 2u * STAGE_C : 0u);   // split-K inside a cluster: receive region
+  const uint32_t bars = sR + (SPLITK == kSplitCluster ? p.kc_recv_bytes : 0u);
   const uint32_t full0 = bars;
   const uint32_t empty0 = bars + 8u * p.stages;
   const uint32_t tfull0 = bars + 16u * p.stages;
   const uint32_t tempty0 = tfull0 + 16u;
   const uint32_t drain = tempty0 + 16u;
   const uint32_t tslot = drain + 8u;
+  const uint32_t recvbar = tslot + 8u;   // split-K inside a cluster: the other splits' sums of this CTA's chunks
   volatile uint32_t* tslot_ptr = reinterpret_cast<volatile uint32_t*>(smem_raw + (tslot - raw));
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const uint32_t rank = p.cl > 1 ? cluster_ctarank() : 0u;
-  const int cid = static_cast<int>(blockIdx.x) / p.cl;
+  // Launched clusters are CTA pairs (PAIRED: rank = the pair's row half) or, for split-K inside a cluster, the kc
+  // splits of one tile (ks = the CTA's split; the host never combines the two).
+  constexpr bool kcl = SPLITK == kSplitCluster;
+  const int ccl = kcl ? p.kc : p.cl;
+  const uint32_t crank = ccl > 1 ? cluster_ctarank() : 0u;
+  const uint32_t rank = kcl ? 0u : crank;
+  const int ks = static_cast<int>(crank);
+  const int cid = static_cast<int>(blockIdx.x) / ccl;
   const bool leader = !PAIRED || rank == 0;
+  bool kc_waiting = false;   // an epilogue warp whose wait for the other splits' sums timed out (see teardown)
   const uint64_t budget = p.budget_ns;
   FirstTile first;
   first.load(p, cid);
@@ -283,7 +300,11 @@ __global__ void __launch_bounds__(kWsThreads, 1)
       mbar_init(tempty0 + 8u * b, 4 * CG);   // one arrival per epilogue warp of each CTA of the pair
     }
     mbar_init(drain, 1);
+    if (kcl) mbar_init(recvbar, 1);
     fence_mbar_init();
+    // the receive barrier's only arrival, with every byte the other splits will send (they may land first: the
+    // phase cannot complete before this arrival)
+    if (kcl) mbar_arrive_expect_tx(recvbar, p.kc_recv_bytes);
   }
   if (warp == 0 && lane == 0) {
     tma_prefetch_map(&tmA);
@@ -297,7 +318,7 @@ __global__ void __launch_bounds__(kWsThreads, 1)
   }
   tc_fence_before();
   __syncthreads();
-  if (PAIRED) cluster_sync_all();   // the peer's barriers and TMEM exist before anyone signals them
+  if (PAIRED || kcl) cluster_sync_all();   // the peers' barriers and TMEM exist before anyone signals them
   tc_fence_after();
   const uint32_t tmem_base = *tslot_ptr;
 
@@ -323,7 +344,7 @@ __global__ void __launch_bounds__(kWsThreads, 1)
       const int row_a = (cm * p.cl + static_cast<int>(rank)) * BM;
       const int row_b = tn * width + (PAIRED ? static_cast<int>(rank) * (bsub / 2) : 0);
       int kb0, nk;
-      k_range<SPLITK>(p, idx, kb0, nk);
+      k_range<SPLITK>(p, idx, ks, kb0, nk);
       // K serpentine: consecutive tiles of a cluster walk K in opposite directions, so a wave of tiles starts on
       // the K-slabs the previous wave read last, which are still in L2 (fewer DRAM reads, less power under the
       // cap). The MMA side counts k-blocks from the first one issued, whichever the direction.
@@ -462,7 +483,7 @@ __global__ void __launch_bounds__(kWsThreads, 1)
         const int nblk = (narrow && NB == 2) ? 1 : NB;
         const uint32_t idesc = (narrow && NB == 1) ? p.idesc_narrow : p.idesc;
         int kb0, nk;   // the MMAs count k-blocks from 0 within the entry's K range: the first one overwrites D
-        k_range<SPLITK>(p, idx, kb0, nk);
+        k_range<SPLITK>(p, idx, ks, kb0, nk);
         if (!split) {
           if (!wait_acc(tempty0 + 8u * acc, acc_phase ^ 1u, i)) break;
           const uint32_t d = tmem_base + acc * static_cast<uint32_t>(p.acc_stride);
@@ -821,26 +842,91 @@ __global__ void __launch_bounds__(kWsThreads, 1)
     // the cluster's last entry is complete (no loads follow, and the MMAs that read it have finished).
     const bool sk_ring_ok =
         static_cast<uint32_t>(p.stages) * (p.a_stage_bytes + p.b_stage_bytes) >= 4u * kSkSlots * 4096u;
+    // Split-K inside a cluster (p.kc > 1): the cluster's kc CTAs hold the partial sums of one tile over disjoint K
+    // ranges (split = cluster rank), and the tile's nch 32-column chunks are shared out, CTA g owning chunks
+    // [g * per, (g + 1) * per). Each CTA sends every chunk it does not own from tensor memory straight into the
+    // owner's receive region (st.async into the owner's shared memory, completing on the owner's receive barrier),
+    // then waits (bounded) for the other kc - 1 CTAs' copies of its own chunks, adds them in split order
+    // 0, 1, ..., kc - 1 (the order of the workspace protocols below, so the same bits), writes the sums back to
+    // tensor memory and drains them to C. Receive region: slot j (the j-th other split in rank order) holds for each
+    // warp q and owned chunk cc one 4 KB unit, in which lane l's 16-byte piece e (columns 4e..4e+3 of its row) sits
+    // at e * 512 + l * 16: sender and owner lanes both move 512 contiguous bytes per instruction. No workspace, no
+    // global-memory round trip: the exchange costs one pass through each SM's shared-memory intake.
+    auto kc_epilogue = [&](int i, uint32_t tacc, int nch, int row0, int col0) {
+      const int per = nch / p.kc;
+      const uint32_t piece = static_cast<uint32_t>(lane) * 16u;
+#pragma unroll 1
+      for (int c = 0; c < nch; ++c) {
+        const int g = c / per;   // the chunk's owner
+        if (g == ks) continue;
+        const int j = ks < g ? ks : ks - 1;   // this CTA's slot in the owner's receive region
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(tacc + 32u * c, v);
+        tmem_ld_wait();
+        const uint32_t unit = sR + static_cast<uint32_t>(((j * 4 + q) * per + (c - g * per)) * 4096) + piece;
+        const uint32_t dst = mapa_shared(unit, static_cast<uint32_t>(g));
+        const uint32_t bar = mapa_shared(recvbar, static_cast<uint32_t>(g));
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+          st_async_v4(dst + 512u * e, v[4 * e], v[4 * e + 1], v[4 * e + 2], v[4 * e + 3], bar);
+      }
+      if (!mbar_wait_warp(recvbar, 0, budget)) {
+        if (lane == 0) record_error(p.err, kErrSplitK, i);
+        kc_waiting = true;
+        return false;
+      }
+      const int lo = ks * per;
+#pragma unroll 1
+      for (int cc = 0; cc < per; ++cc) {
+        float a[32];
+#pragma unroll 1
+        for (int s = 0; s < p.kc; ++s) {
+          uint32_t x[32];
+          if (s == ks) {
+            tmem_ld_32x32b_x32(tacc + 32u * (lo + cc), x);
+            tmem_ld_wait();
+          } else {
+            const int j = s < ks ? s : s - 1;
+            const uint32_t unit = sR + static_cast<uint32_t>(((j * 4 + q) * per + cc) * 4096) + piece;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) ld_shared_v4(unit + 512u * e, x[4 * e], x[4 * e + 1], x[4 * e + 2], x[4 * e + 3]);
+          }
+#pragma unroll
+          for (int e = 0; e < 32; ++e) a[e] = s == 0 ? __uint_as_float(x[e]) : a[e] + __uint_as_float(x[e]);
+        }
+        uint32_t w[32];
+#pragma unroll
+        for (int e = 0; e < 32; ++e) w[e] = __float_as_uint(a[e]);
+        tmem_st_32x32b_x32(tacc + 32u * (lo + cc), w);
+      }
+      tmem_st_wait();
+      drain(tacc + 32u * lo, row0, col0 + 32 * lo, 32 * per, 0u);
+      return true;
+    };
     // The split-K epilogue of entry idx, whose accumulator (nch chunks at TMEM tacc) is complete. False on timeout.
-    auto sk_epilogue = [&](int idx, int i, uint32_t tacc, int nch, int row0, int col0) {
-      sk_setup(idx);
-      const bool staged = sk_ring_ok && idx + p.nclusters >= p.tiles;
-      if (p.sk_scatter) {
-        const int lo = sk_own * nch / p.split_k, hi = (sk_own + 1) * nch / p.split_k;
-        sk_publish(tacc, nch, lo, hi);
-        if (!sk_count_all(i)) return false;
-        sk_reduce(tacc, lo, hi, staged, p.C + static_cast<long long>(row0 + lane) * p.ldc + col0,
-                  lane < ROWS_W && row0 + lane < p.m_valid, p.n_valid - col0);
-        sk_leave();
+    auto sk_epilogue = [&](int idx, int i, uint32_t tacc, int nch, int row0, int col0) -> bool {
+      if constexpr (kcl) {
+        return kc_epilogue(i, tacc, nch, row0, col0);
+      } else {
+        sk_setup(idx);
+        const bool staged = sk_ring_ok && idx + p.nclusters >= p.tiles;
+        if (p.sk_scatter) {
+          const int lo = sk_own * nch / p.split_k, hi = (sk_own + 1) * nch / p.split_k;
+          sk_publish(tacc, nch, lo, hi);
+          if (!sk_count_all(i)) return false;
+          sk_reduce(tacc, lo, hi, staged, p.C + static_cast<long long>(row0 + lane) * p.ldc + col0,
+                    lane < ROWS_W && row0 + lane < p.m_valid, p.n_valid - col0);
+          sk_leave();
+          return true;
+        }
+        sk_publish(tacc, nch, 0, 0);
+        if (sk_count()) {
+          sk_reduce(tacc, 0, nch, staged, nullptr, false, 0);
+          tmem_st_wait();
+          drain(tacc, row0, col0, nch * 32, 0u);
+        }
         return true;
       }
-      sk_publish(tacc, nch, 0, 0);
-      if (sk_count()) {
-        sk_reduce(tacc, 0, nch, staged, nullptr, false, 0);
-        tmem_st_wait();
-        drain(tacc, row0, col0, nch * 32, 0u);
-      }
-      return true;
     };
     for (int i = 0;; ++i) {
       const int idx = cid + i * p.nclusters;
@@ -905,7 +991,10 @@ __global__ void __launch_bounds__(kWsThreads, 1)
   // ------------------------------------------------------------------ teardown
   tc_fence_before();
   __syncthreads();
-  if (PAIRED) cluster_sync_all();   // the pair is done with each other's barriers and tensor memory
+  if (PAIRED || kcl) cluster_sync_all();   // the cluster is done with each other's barriers and memory
+  // A wait for the other splits' sums that timed out: every CTA of the cluster has now passed the barrier, so the
+  // stores it sends here have been issued; let them land (bounded) before this CTA's shared memory goes away.
+  if (kc_waiting && lane == 0) mbar_wait_bounded(recvbar, 0, budget);
   tc_fence_after();
   if (warp == 1) {
     __syncwarp();

@@ -175,6 +175,16 @@ __device__ __forceinline__ void st_global_v4(void* ptr, uint32_t a, uint32_t b, 
   asm volatile("st.global.v4.b32 [%0], {%1, %2, %3, %4};" ::"l"(ptr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
 }
 
+// 16 bytes into another CTA's shared memory (both addresses in the shared::cluster window, via mapa_shared): the
+// store completes 16 bytes of transaction count on `remote_bar`, a barrier of the destination CTA, whose phase
+// completion then makes the data visible to the threads that wait on it.
+__device__ __forceinline__ void st_async_v4(uint32_t remote_addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d,
+                                            uint32_t remote_bar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.b32 [%0], {%1, %2, %3, %4}, [%5];"
+               ::"r"(remote_addr), "r"(a), "r"(b), "r"(c), "r"(d), "r"(remote_bar)
+               : "memory");
+}
+
 // Split-K partial sums travel between SMs within one launch: their loads go through L2 only (.cg), since L1 is
 // not coherent across SMs. cp_async_16 is the asynchronous form (global -> this CTA's shared memory, 16 bytes, no
 // registers held while in flight); each commit closes a group, and wait_group<N> returns once at most N of this

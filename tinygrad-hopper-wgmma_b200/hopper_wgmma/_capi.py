@@ -26,7 +26,8 @@ class BgCfg(ctypes.Structure):
               ("hilbert", ctypes.c_int32), ("acc_bufs", ctypes.c_int32), ("wait_budget_ns", ctypes.c_int64),
               ("debug_skip_job", ctypes.c_int32), ("n_mma", ctypes.c_int32),
               ("no_tail_split", ctypes.c_int32), ("ragged", ctypes.c_int32), ("split_k", ctypes.c_int32),
-              ("no_k_serpentine", ctypes.c_int32), ("b_nmajor", ctypes.c_int32), ("wave_sync", ctypes.c_int32)]
+              ("no_k_serpentine", ctypes.c_int32), ("b_nmajor", ctypes.c_int32), ("wave_sync", ctypes.c_int32),
+              ("split_k_cluster", ctypes.c_int32)]
 
 
 class BgPlanInfo(ctypes.Structure):

@@ -165,6 +165,9 @@ class WSCfg:
                                # in step so that they share operand panels through L2: True = on, False = off,
                                # None = on when each cluster runs >= 4 tiles and a wave's K-long operand panels
                                # outgrow L2 (256x512 pair tiles from K = 8192; no split-K)
+  split_k_cluster: bool | None = None  # how split-K meets: True = the splits of a tile are the CTAs of one cluster
+                               # and add up through distributed shared memory (single-CTA tiles, split_k 2 or 4, one
+                               # wave), False = through a global fp32 workspace, None = the cluster where it applies
 
   def __post_init__(self):
     if self.BK != 64: raise ValueError("BK must be 64 (one 128-byte swizzle atom)")
@@ -205,7 +208,7 @@ class WSCfg:
   @property
   def stage_bytes(self): return (self.a_elems + self.b_elems) * 2 + Ring.BYTES_PER_STAGE
   @property
-  def fixed_bytes(self): return SMEM_ALIGN_SLACK + self.c_elems * 2 + 48   # + accumulator/drain barriers, TMEM slot
+  def fixed_bytes(self): return SMEM_ALIGN_SLACK + self.c_elems * 2 + 56   # + accumulator/drain/receive barriers, TMEM slot
   @property
   def stages_used(self):
     if self.stages is not None: return self.stages
@@ -243,7 +246,8 @@ class WSCfg:
             f"{f'_r{self.regs[0]}x{self.regs[1]}' if self.regs else ''}{f'_cl{self.cluster}' if self.cluster > 1 else ''}"
             f"{f'_x{self.n_mma}' if self.n_mma > 1 else ''}{f'_sk{self.split_k}' if self.split_k > 1 else '_skA' if self.split_k == -1 else ''}"
             f"{'' if self.k_serpentine else '_kfwd'}{'' if self.b_nmajor is None else '_bN' if self.b_nmajor else '_bT'}"
-            f"{'' if self.wave_sync is None else '_wsync' if self.wave_sync else '_nowsync'}")
+            f"{'' if self.wave_sync is None else '_wsync' if self.wave_sync else '_nowsync'}"
+            f"{'' if self.split_k_cluster is None else '_skc' if self.split_k_cluster else '_skw'}")
 
   def to_c(self, kind: int = _capi.KIND_WS, num_sm: int | None = None, wait_budget_ns: int = 0,
            debug_skip_job: int = -1, b_nmajor: bool = False) -> _capi.BgCfg:
@@ -254,7 +258,8 @@ class WSCfg:
                        acc_bufs=self.acc_bufs or 0, wait_budget_ns=wait_budget_ns, debug_skip_job=debug_skip_job,
                        n_mma=self.n_mma, no_tail_split=0 if self.split_tail else 1, ragged=int(self.ragged),
                        split_k=self.split_k, no_k_serpentine=0 if self.k_serpentine else 1,
-                       b_nmajor=int(b_nmajor), wave_sync={None: 0, True: 1, False: 2}[self.wave_sync])
+                       b_nmajor=int(b_nmajor), wave_sync={None: 0, True: 1, False: 2}[self.wave_sync],
+                       split_k_cluster={None: 0, True: 1, False: 2}[self.split_k_cluster])
 
 
 # =============================================================================================================

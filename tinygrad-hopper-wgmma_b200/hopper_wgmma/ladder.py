@@ -69,7 +69,8 @@ def lookup(name: str):
   to a K-major BT first (``b_nmajor=False``, the reference's operand layout), ``@bN`` makes it read B[K,N]
   directly wherever the tile allows (``b_nmajor=True``) and ``@g<M>x<N>`` replaces the tile order by the grouped
   order with ``group_m=M, group_n=N`` (``hilbert=False``); ``@wsync`` / ``@nowsync`` force the wave barrier
-  on or off (``wave_sync``). Example: ``cta_n128@sk2``, ``cta_n64@reg@skA``,
+  on or off (``wave_sync``); ``@skc`` / ``@skw`` make split-K meet inside a cluster or through the workspace
+  (``split_k_cluster``). Example: ``cta_n128@sk2``, ``cta_n128@sk2@skw``, ``cta_n64@reg@skA``,
   ``pair_n128@s4``, ``cluster_hilbert@bT``, ``cta_n128@bN``, ``pair_wide@g64x8``."""
   import dataclasses
   base, *mods = name.split("@")
@@ -78,6 +79,8 @@ def lookup(name: str):
     if not isinstance(cfg, WSCfg): raise ValueError(f"{base} is not a persistent config: no @{mod}")
     if mod == "reg":
       cfg = dataclasses.replace(cfg, tma_store=False)
+    elif mod in ("skc", "skw"):
+      cfg = dataclasses.replace(cfg, split_k_cluster=mod == "skc")
     elif mod.startswith("sk") and (mod[2:].isdigit() or mod[2:] == "A"):
       cfg = dataclasses.replace(cfg, split_k=-1 if mod[2:] == "A" else int(mod[2:]))
     elif mod in ("bT", "bN"):
