@@ -436,6 +436,21 @@ class Bench:
     steps = max(3, min(self.args.steps, 30))
     for i in range(2 * nsets): step(i)
     torch.cuda.synchronize()
+    # the copies alone, one direction at a time on one stream: the bound the end-to-end step cannot beat (its
+    # device-to-host copies overlap the next steps' host-to-device copies)
+    hA, hB, hC, dA, dB, dC, st = sets[0]
+    rates = {}
+    for name, copies, nbytes in (("h2d", ((dA, hA), (dB, hB)), 2 * (M * K + K * n)), ("d2h", ((hC, dC),), 2 * M * n)):
+      e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+      with torch.cuda.stream(st):
+        for dst, src in copies: dst.copy_(src, non_blocking=True)
+        e0.record(st)
+        for _ in range(3):
+          for dst, src in copies: dst.copy_(src, non_blocking=True)
+        e1.record(st)
+      st.synchronize()
+      rates[name] = 3 * nbytes / (e0.elapsed_time(e1) * 1e-3) / 1e9
+    copy_bound_ms = max(2 * (M * K + K * n) / rates["h2d"], 2 * M * n / rates["d2h"]) / 1e6
     self.barrier()
     cur = torch.cuda.current_stream(self.dev)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -456,7 +471,9 @@ class Bench:
             "path": "pinned host A,B -> build_gemm_ws(...)(A, B, C)() ("
                     f"{'B read N-major as given' if cfg.reads_b_directly else 'K-major copy of B'}, plan, launch) -> "
                     f"pinned host C; {nsets} streams and buffer sets, steps overlapped",
-            "steps": steps, "ms_per_step": round(e2e_ms / steps, 4)}
+            "steps": steps, "ms_per_step": round(e2e_ms / steps, 4),
+            "h2d_gbs": round(rates["h2d"], 1), "d2h_gbs": round(rates["d2h"], 1),
+            "copy_bound_ms": round(copy_bound_ms, 4), "frac_of_copy_bound": round(copy_bound_ms / (e2e_ms / steps), 3)}
 
   def allgather(self, C, M, n):
     """Optional NCCL all-gather of the C shards over NVLink (A replicated, B and C column-sharded): timed

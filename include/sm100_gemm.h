@@ -67,7 +67,7 @@ enum {
  *   debug_skip_job  test hook: the producer never loads this job (-1 = off) so that the kernel's waits run out and
  *                   the launch reports an error instead of hanging
  *   split_k     0 or 1: off. -1: automatic (the most splits, up to 16, that keep all tiles' splits within one wave of
- *               clusters with at least 32 k-blocks each; off otherwise).
+ *               clusters with at least 32 k-blocks each, 24 where they can meet inside a cluster; off otherwise).
  *               S in [2, 64] (persistent kernel, tiles a multiple of 32 columns wide, S <= K / 64):
  *               each output tile is computed by S entries of the schedule, each over a contiguous 1/S of K, on
  *               different clusters; fp32 partial sums meet in a plan-owned workspace and are added in split

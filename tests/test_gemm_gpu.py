@@ -435,7 +435,7 @@ def test_split_k_timeout_reports_error_and_plans_recover(cuda_dev):
 
 def test_split_k_auto_choice(cuda_dev):
   """split_k=-1 splits only shapes with few tiles and long K: as many splits as keep one wave of clusters, each
-  with at least 32 k-blocks."""
+  with at least 32 k-blocks, or 24 where the splits meet inside a cluster."""
   from hopper_wgmma import WSCfg, build_gemm_ws
   from hopper_wgmma._capi import device_info
   sms = device_info(cuda_dev.index or 0)["sm_count"]
@@ -447,6 +447,13 @@ def test_split_k_auto_choice(cuda_dev):
   _, launch = run_case(lambda: build_gemm_ws(1024, cfg, 1024, 1024, wait_budget_ns=BUDGET_NS), 1024, 1024, 1024,
                        cuda_dev, reps=1)
   assert launch.info()["split_k"] == 1            # 16 k-blocks: too short to split
+  cfg = WSCfg(BN=128, tma_store=True, split_k=-1)
+  M, N, K = 1024, 1024, 3072                      # 64 tiles, 48 k-blocks: two splits of 24 inside clusters
+  worst, launch = run_case(lambda: build_gemm_ws(N, cfg, M, K, wait_budget_ns=BUDGET_NS), M, N, K, cuda_dev, reps=2)
+  assert worst <= TOL
+  assert launch.info()["split_k"] == 2 and "splitk=2/cluster" in launch.info()["kernel"]
+  _, launch = run_case(lambda: build_gemm_ws(N, cfg, M, 2048, wait_budget_ns=BUDGET_NS), M, N, 2048, cuda_dev, reps=1)
+  assert launch.info()["split_k"] == 1            # 32 k-blocks: splits of 16 gain nothing
 
 
 # ------------------------------------------------------------------------------------------------------------------

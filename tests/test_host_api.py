@@ -320,3 +320,38 @@ def test_ragged_shape_contract():
     build_gemm_ws(522, WSCfg(ragged=True), 300, 200)
   with pytest.raises(ValueError, match="multiples of 8"):
     build_gemm_ws(520, WSCfg(ragged=True), 300, 201)
+
+
+@pytest.mark.parametrize("splits,width", [(2, 64), (2, 128), (2, 256), (4, 128), (4, 256)])
+def test_split_k_cluster_exchange_layout(splits, width):
+  """The index arithmetic of the cluster split-K exchange (kc_epilogue in csrc/gemm_kernels.cuh), checked on the
+  host: every 16-byte piece a CTA sends lands inside its owner's receive region ((splits - 1) x 128 lanes x
+  width / splits x 4 bytes, the host's expect_tx count) at an offset no other piece uses, the owner reads each piece
+  at the offset it was written to, and the owner sees every other split exactly once per owned chunk."""
+  nch = width // 32
+  per = nch // splits
+  recv_bytes = (splits - 1) * 128 * (width // splits) * 4
+  written = {}   # (owner, byte offset) -> (sender, chunk, warp, lane, piece)
+  for ks in range(splits):                       # sender: its chunks owned by others
+    for c in range(nch):
+      g = c // per
+      if g == ks: continue
+      j = ks if ks < g else ks - 1
+      for q in range(4):
+        for lane in range(32):
+          for e in range(8):
+            off = ((j * 4 + q) * per + (c - g * per)) * 4096 + lane * 16 + 512 * e
+            assert 0 <= off and off + 16 <= recv_bytes
+            assert (g, off) not in written
+            written[(g, off)] = (ks, c, q, lane, e)
+  assert len(written) * 16 == splits * recv_bytes   # every byte of every receive region is written once
+  for g in range(splits):                         # owner: its chunks, the other splits in split order
+    for cc in range(per):
+      for s in range(splits):
+        if s == g: continue
+        j = s if s < g else s - 1
+        for q in range(4):
+          for lane in range(32):
+            for e in range(8):
+              off = ((j * 4 + q) * per + cc) * 4096 + lane * 16 + 512 * e
+              assert written[(g, off)] == (s, g * per + cc, q, lane, e)

@@ -594,12 +594,19 @@ int32_t setup_plan(const bg_cfg& c, int64_t M, int64_t N, int64_t K, const void*
 
   // ---- automatic split-K: the most splits that still fit the tiles in one wave of clusters
   // (num_sm / cluster of them), each split keeping at least kAutoSplitMinKb k-blocks (below that the partial-sum
-  // round trip costs more than the split saves)
+  // round trip costs more than the split saves), or kAutoSplitMinKbCluster where the splits can meet inside a
+  // cluster (single-CTA tiles, 2 or 4 splits, each split's share of the columns whole 64- or 32-column chunks):
+  // CUDA events, L2 flushed, 128x128 tiles with 2 splits inside a cluster against none: 16 k-blocks per split
+  // even (1024x1024x2048, 512x512x2048), 24 per split 10 % faster (1024x1024x3072)
   if (sk_auto && c.kind == BG_KIND_WS && width % 32 == 0) {
-    constexpr int kAutoSplitMinKb = 32, kAutoSplitMax = 16;
-    for (int s2 = 2; s2 <= kAutoSplitMax; ++s2)
-      if (tiles * s2 <= nclusters && nkb >= static_cast<int64_t>(kAutoSplitMinKb) * s2 && nkb * s2 <= (1ll << 30))
-        sk = s2;
+    constexpr int kAutoSplitMinKb = 32, kAutoSplitMinKbCluster = 24, kAutoSplitMax = 16;
+    const int num_sm = c.num_sm > 0 ? c.num_sm : sm_count;
+    for (int s2 = 2; s2 <= kAutoSplitMax; ++s2) {
+      const bool in_cluster = c.split_k_cluster != 2 && cl == 1 && nblk == 1 && (s2 == 2 || s2 == 4) &&
+                              width % s2 == 0 && (width / s2) % (c.tma_store ? 64 : 32) == 0 && tiles * s2 <= num_sm;
+      const int min_kb = in_cluster ? kAutoSplitMinKbCluster : kAutoSplitMinKb;
+      if (tiles * s2 <= nclusters && nkb >= static_cast<int64_t>(min_kb) * s2 && nkb * s2 <= (1ll << 30)) sk = s2;
+    }
   }
 
   // ---- kernel and launch attributes
@@ -720,6 +727,10 @@ int32_t setup_plan(const bg_cfg& c, int64_t M, int64_t N, int64_t K, const void*
     p->max_active_clusters = maxc;
     if (c.kind == BG_KIND_WS) nclusters = std::min<int64_t>(nclusters, maxc);
   }
+  // split-K inside a cluster runs exactly one tile per cluster (its receive barrier serves one phase)
+  if (kc > 1 && nclusters < tiles)
+    return fail(5, "split-K inside a cluster: %lld tiles but only %lld clusters of %d fit", (long long)tiles,
+                (long long)nclusters, lcl);
   // ---- wave-quantization tail: the last, partial wave of the persistent schedule (entries [full, tiles) of the
   // dealt table) is split into half-width tiles when twice its size still fits in one wave, so that the tail takes
   // about half a tile's time instead of a whole one. Half width = one N block when nblk == 2, MMA N = BN/2 otherwise.
