@@ -436,21 +436,33 @@ class Bench:
     steps = max(3, min(self.args.steps, 30))
     for i in range(2 * nsets): step(i)
     torch.cuda.synchronize()
-    # the copies alone, one direction at a time on one stream: the bound the end-to-end step cannot beat (its
-    # device-to-host copies overlap the next steps' host-to-device copies)
+    # The copies without the GEMM: each direction alone on one stream, then both directions at once on two streams
+    # (a step's device-to-host copy overlaps the next steps' host-to-device copies), whose time per step is the
+    # bound the end-to-end step cannot beat.
     hA, hB, hC, dA, dB, dC, st = sets[0]
+    st2 = sets[1][6]
+    h2d, d2h = ((dA, hA), (dB, hB)), ((hC, dC),)
     rates = {}
-    for name, copies, nbytes in (("h2d", ((dA, hA), (dB, hB)), 2 * (M * K + K * n)), ("d2h", ((hC, dC),), 2 * M * n)):
+
+    def timed(plan):   # plan: [(stream, copies)]; three rounds after one untimed round, seconds per round
+      cur = torch.cuda.current_stream(self.dev)
       e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-      with torch.cuda.stream(st):
-        for dst, src in copies: dst.copy_(src, non_blocking=True)
-        e0.record(st)
-        for _ in range(3):
-          for dst, src in copies: dst.copy_(src, non_blocking=True)
-        e1.record(st)
-      st.synchronize()
-      rates[name] = 3 * nbytes / (e0.elapsed_time(e1) * 1e-3) / 1e9
-    copy_bound_ms = max(2 * (M * K + K * n) / rates["h2d"], 2 * M * n / rates["d2h"]) / 1e6
+      for rounds, ev in ((1, None), (3, e0)):
+        if ev is not None:
+          torch.cuda.synchronize()
+          ev.record(cur)
+        for s, copies in plan:
+          s.wait_stream(cur)
+          with torch.cuda.stream(s):
+            for _ in range(rounds):
+              for dst, src in copies: dst.copy_(src, non_blocking=True)
+        for s, _ in plan: cur.wait_stream(s)
+      e1.record(cur)
+      torch.cuda.synchronize()
+      return e0.elapsed_time(e1) * 1e-3 / 3
+    rates["h2d"] = 2 * (M * K + K * n) / timed([(st, h2d)]) / 1e9
+    rates["d2h"] = 2 * M * n / timed([(st, d2h)]) / 1e9
+    copy_bound_ms = timed([(st, h2d), (st2, d2h)]) * 1e3
     self.barrier()
     cur = torch.cuda.current_stream(self.dev)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
