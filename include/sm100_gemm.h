@@ -12,9 +12,11 @@
  *
  * Threading: a plan is immutable after bg_plan_create and may be launched repeatedly on one stream at a time. Plans
  * on different devices or streams are independent. Launches are asynchronous on the given stream. One exception: a
- * split-K plan whose splits all run in one wave (the splits of a tile wait for each other) needs all its CTAs
- * resident at once; launched beside other work that holds SMs, its bounded wait can run out, and the launch then
- * reports an error (bg_plan_check_error) instead of a result.
+ * split-K plan that reduces through the workspace with all its splits in one wave (the splits of a tile wait for
+ * each other on different clusters) needs all its CTAs resident at once; launched beside other work that holds SMs,
+ * its bounded wait can run out, and the launch then reports an error (bg_plan_check_error) instead of a result.
+ * Split-K inside a cluster has no such need: the CTAs that wait for each other form one cluster, which the GPU
+ * always schedules at once.
  */
 #ifndef SM100_GEMM_H
 #define SM100_GEMM_H
