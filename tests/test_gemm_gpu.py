@@ -711,3 +711,32 @@ def test_wave_sync_launches_side_by_side_on_two_streams(cuda_dev):
     with torch.cuda.stream(st):
       launch.check()
     assert gemm_ref.rel_err(to_bits(C), gemm_ref.gemm_f32(a_bits, b_bits)) <= TOL
+
+
+def test_split_k_cluster_launches_side_by_side_on_two_streams(cuda_dev):
+  """Two split-K-inside-a-cluster launches of 128 CTAs each on two streams at once (more CTAs than SMs together):
+  only a cluster's own CTAs wait for each other, and the GPU schedules a cluster whole, so both finish correctly
+  without a timeout."""
+  torch = _torch()
+  from hopper_wgmma import WSCfg, build_gemm_ws
+  from oracle import gemm_ref
+  M, N, K = 1024, 1024, 2048
+  cfg = WSCfg(BN=128, tma_store=True, split_k=2, split_k_cluster=True)   # 64 tiles x 2 splits
+  runs = []
+  for seed in (40, 41):
+    a_bits, b_bits = inputs(M, N, K, seed=seed)
+    A, B = to_dev(a_bits, cuda_dev), to_dev(b_bits, cuda_dev)
+    C = torch.empty((M, N), dtype=torch.bfloat16, device=cuda_dev)
+    poison(C)
+    runs.append((a_bits, b_bits, C, build_gemm_ws(N, cfg, M, K, wait_budget_ns=BUDGET_NS)(A, B, C)))
+  assert "splitk=2/cluster" in runs[0][3].info()["kernel"] and runs[0][3].info()["grid"] == 128
+  streams = [torch.cuda.Stream(device=cuda_dev) for _ in runs]
+  torch.cuda.synchronize(cuda_dev)
+  for _ in range(5):
+    for st, (_, _, _, launch) in zip(streams, runs):
+      with torch.cuda.stream(st):
+        launch()
+  for st, (a_bits, b_bits, C, launch) in zip(streams, runs):
+    with torch.cuda.stream(st):
+      launch.check()
+    assert gemm_ref.rel_err(to_bits(C), gemm_ref.gemm_f32(a_bits, b_bits)) <= TOL
