@@ -473,10 +473,13 @@ def _split_k_cluster_cases():
     ("ragged_sk2", WSCfg(BN=128, tma_store=True, ragged=True, split_k=2, split_k_cluster=True), (300, 520, 1000)),
     ("one_kblock_each_sk4", WSCfg(BN=256, tma_store=True, split_k=4, split_k_cluster=True), (128, 256, 256)),
     ("auto_picks_cluster", WSCfg(BN=128, tma_store=True, split_k=2), (384, 512, 2048)),
+    ("bm64_reg_sk2", WSCfg(consumers=1, BN=128, split_k=2, split_k_cluster=True), (256, 256, 512)),
+    ("bn192_reg_sk2_three_chunks_each", WSCfg(BN=192, split_k=2, split_k_cluster=True), (256, 384, 512)),
+    ("ragged_reg_sk4", WSCfg(BN=256, ragged=True, split_k=4, split_k_cluster=True), (200, 600, 904)),
   ]
 
 
-@pytest.mark.parametrize("idx", range(10))
+@pytest.mark.parametrize("idx", range(13))
 def test_split_k_in_cluster(idx, cuda_dev):
   """Three launches of one plan on NaN-poisoned C, against the CPU oracle: every tile's splits run on one cluster and
   exchange their sums through distributed shared memory (the plan's kernel name says so)."""
